@@ -1,0 +1,358 @@
+"""Benchmark of the selectssm selective-scan hot path on B200.
+
+Metric: scan fwd+bwd tokens*channels/s and % of the HBM roofline.
+Workload at N=1: config 2 of the benchmark contract -- the raw selective-scan op
+forward + backward in float32, batch=8, L=4096, d_inner=1536, N=16, with the
+softplus(dt) preamble, D skip and silu(z) gate fused in; synthetic seeded inputs
+(u, z ~ N(0,1); dt_raw ~ N(0,1) - 4; A = -U[1,16]; B, C ~ N(0,1); D ~ N(1, 0.1);
+upstream grad ~ N(0,1)).  One step = one forward + one backward over the batch.
+
+Multi-GPU (torchrun, one process per GPU): weak scaling, each rank scans its own
+batch of 8 sequences (batch sharding, no collective in the forward) and the
+backward ends with one NCCL all-reduce of the small parameter gradients
+(dA, dD) -- the only exchange the partition needs.
+
+`--impl reference` times the reference algorithm on the host CPU instead: the
+NumPy restatement of ssm_chunked_scan (forward) and of the ssm_scan custom-VJP
+backward from oracle/, on a bounded prefix of the same workload (JAX, the
+reference's own runtime, is not installed on this image).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+CFG = dict(batch=8, seqlen=4096, dim=1536, dstate=16)
+METRIC = "scan fwd+bwd tokens*channels/s (and % HBM roofline)"
+UNIT = "tokens*channels/s"
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            j = json.load(f)
+        return float(j["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def alg_bytes(units, s, N, D):
+    """Algorithmic HBM bytes: forward reads u, dt, z and writes y (4s per unit);
+    backward reads u, dt, z, dy and writes du, ddt, dz (7s); B and C are read by
+    both and dB, dC written (6 s N per (b,l), amortised over D channels)."""
+    fwd = units * (4 * s + 2 * s * N / D)
+    bwd = units * (7 * s + 4 * s * N / D)
+    return fwd, bwd
+
+
+def read_traffic(name):
+    """dram bytes per launch recorded in a committed ncu summary, else None."""
+    p = os.path.join(ROOT, "profiles", name)
+    try:
+        with open(p) as f:
+            for line in f:
+                if line.startswith("traffic_bytes_per_launch:"):
+                    return float(line.split(":", 1)[1])
+    except OSError:
+        pass
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle samples every 200 ms while running."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.rows = []
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9:
+                self.rows.append(parts)
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in self.rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.rows)}
+
+
+# ----------------------------------------------------------------------------- inputs
+def host_inputs(seed, B, L, D, N):
+    """Seeded float32 host inputs of config 2 (one generator per tensor)."""
+    ss = np.random.SeedSequence(seed).spawn(8)
+    g = [np.random.default_rng(s) for s in ss]
+    f32 = np.float32
+    return dict(
+        u=g[0].standard_normal((B, L, D), dtype=f32),
+        z=g[1].standard_normal((B, L, D), dtype=f32),
+        delta=(g[2].standard_normal((B, L, D), dtype=f32) - f32(4.0)),
+        A=(-g[3].uniform(1.0, 16.0, size=(D, N))).astype(f32),
+        B=g[4].standard_normal((B, L, N), dtype=f32),
+        C=g[5].standard_normal((B, L, N), dtype=f32),
+        D=(1.0 + 0.1 * g[6].standard_normal(D)).astype(f32),
+        dout=g[7].standard_normal((B, L, D), dtype=f32),
+    )
+
+
+# ----------------------------------------------------------------------------- CPU arm
+def cpu_reference_step(inp, chunk_size=None):
+    """One fwd+bwd of the fused op with the restated reference algorithm:
+    ssm_chunked_scan forward (selectssm.py:37-109) and the ssm_scan custom-VJP
+    backward (ssmrecscan.py:111-181, default min_recursion_length=2)."""
+    from oracle import selectssm_oracle as O
+    u, delta, z, dout = inp["u"], inp["delta"], inp["z"], inp["dout"]
+    A, Bm, Cm, Dv = inp["A"], inp["B"], inp["C"], inp["D"]
+    dt = O.softplus(delta)
+    ys = O.ssm_chunked_scan(u, A, Bm, Cm, dt, chunk_size)
+    pre = ys + u * Dv
+    g = O.activation(z, "silu")
+    out = pre * g
+    dpre = dout * g
+    dz = dout * pre * O.activation_grad(z, "silu")
+    dx, dA, dB, dC, ddt = O.ssm_scan_backward(u, A, Bm, Cm, dt, dpre)
+    du = dx + dpre * Dv
+    dD = np.einsum("bld,bld->d", dpre, u)
+    ddelta = ddt * O.sigmoid(delta)
+    return out, du, ddelta, dz, dA, dB, dC, dD
+
+
+def cpu_threads():
+    try:
+        from threadpoolctl import threadpool_info
+        n = [i.get("num_threads", 1) for i in threadpool_info()]
+        return max(n) if n else 1
+    except Exception:
+        return 1
+
+
+def run_cpu_sample(seqlen=256, reps=1):
+    B, D, N = 1, CFG["dim"], CFG["dstate"]
+    inp = host_inputs(0, B, seqlen, D, N)
+    cpu_reference_step(inp)  # warm
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        cpu_reference_step(inp)
+    dt = (time.perf_counter() - t0) / reps
+    units = B * seqlen * D
+    sample = (f"NumPy restatement of the reference algorithm (chunked scan fwd + custom-VJP bwd, "
+              f"float32) on a prefix batch=1, L={seqlen}, d_inner={D}, N={N} of the config-2 workload; "
+              f"{reps} rep(s) after 1 warm-up; elementwise work single-threaded, BLAS threads {cpu_threads()}")
+    return units / dt, dt, sample
+
+
+# ----------------------------------------------------------------------------- GPU arm
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--e2e-steps", type=int, default=3)
+    args = ap.parse_args()
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    Bsz, L, D, N = CFG["batch"], CFG["seqlen"], CFG["dim"], CFG["dstate"]
+    config = {"workload": "config 2: raw selective-scan op fwd+bwd (softplus dt, D skip, silu gate fused)",
+              "batch_per_gpu": Bsz, "global_batch": Bsz * world, "seq_len": L, "d_inner": D, "d_state": N,
+              "parallelism": f"batch-sharded dp{world}, NCCL all-reduce of dA/dD in bwd" if world > 1 else "single GPU",
+              "l2": "inputs larger than L2 (u, dt, z, dy = 805 MB per step), no flush"}
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        steps = max(1, args.steps)
+        vals = []
+        for _ in range(args.warmup):
+            run_cpu_sample(seqlen=64)
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            v, _, sample = run_cpu_sample(seqlen=128)
+            vals.append(v)
+        total = time.perf_counter() - t0
+        v = statistics.median(vals)
+        line = {"metric": METRIC, "value": v, "unit": UNIT, "n_gpus": world, "steps": steps,
+                "warmup": args.warmup, "ms_per_step": 1e3 * total / steps, "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": config,
+                "impl": "reference",
+                "cpu_baseline": {"value": v, "unit": UNIT, "cores": cpu_threads(), "kind": "port",
+                                 "sample": sample},
+                "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line))
+        return
+
+    import torch
+    import torch.distributed as dist
+    import selectssm_b200 as S
+    from selectssm_b200 import _lib
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev)
+    lib = _lib.load()
+
+    h = host_inputs(1234 + rank, Bsz, L, D, N)
+    t = {k: torch.from_numpy(v).to(dev) for k, v in h.items()}
+    for k in ("u", "delta", "z", "A", "B", "C", "D"):
+        t[k].requires_grad_(True)
+    launches_per_step = 5  # ssm_fwd: 1; ssm_bwd: 2 zero + 1 scan + 1 finalize
+
+    def step(inputs):
+        for k in ("u", "delta", "z", "A", "B", "C", "D"):
+            inputs[k].grad = None
+        out = S.selective_scan(inputs["u"], inputs["delta"], inputs["A"], inputs["B"], inputs["C"], D=inputs["D"],
+                               z=inputs["z"], delta_softplus=True)
+        out.backward(inputs["dout"])
+        if world > 1:
+            flat = torch.cat([inputs["A"].grad.reshape(-1), inputs["D"].grad.reshape(-1)])
+            dist.all_reduce(flat)
+        return out
+
+    for _ in range(max(3, args.warmup)):
+        step(t)
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local_rank) as clk:
+        e0.record(stream)
+        for _ in range(args.steps):
+            step(t)
+        e1.record(stream)
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    if world > 1:
+        mt = torch.tensor([ms], device=dev)
+        dist.all_reduce(mt, op=dist.ReduceOp.MAX)
+        ms = float(mt.item())
+        dist.barrier()
+
+    units = Bsz * L * D
+    value = units * world / (ms * 1e-3)
+
+    # --- per-kernel timing of the forward and backward calls (same stream)
+    p_fwd, p_bwd = [], []
+    for _ in range(5):
+        a0, a1, a2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+        for k in ("u", "delta", "z", "A", "B", "C", "D"):
+            t[k].grad = None
+        a0.record(stream)
+        out = S.selective_scan(t["u"], t["delta"], t["A"], t["B"], t["C"], D=t["D"], z=t["z"], delta_softplus=True)
+        a1.record(stream)
+        out.backward(t["dout"])
+        a2.record(stream)
+        torch.cuda.synchronize()
+        p_fwd.append(a0.elapsed_time(a1))
+        p_bwd.append(a1.elapsed_time(a2))
+    t_fwd, t_bwd = statistics.median(p_fwd), statistics.median(p_bwd)
+    hbm, src = peaks()
+    fb, bb = alg_bytes(units, 4, N, D)
+    roof_bwd = {"kernel": "ssm_bwd_kernel<float,float> (+2 zero, 1 finalize launch)", "bound": "hbm",
+                "achieved": bb / (t_bwd * 1e-3) / 1e9, "peak": hbm, "unit": "GB/s", "peak_source": src,
+                "traffic": read_traffic("ssm_bwd_kernel_config2.md"), "algorithmic_bytes": bb,
+                "ms": t_bwd}
+    roof_bwd["frac"] = roof_bwd["achieved"] / hbm
+    roof_fwd = {"kernel": "ssm_fwd_kernel<float,float>", "bound": "hbm", "achieved": fb / (t_fwd * 1e-3) / 1e9,
+                "peak": hbm, "unit": "GB/s", "traffic": read_traffic("ssm_fwd_kernel_config2.md"),
+                "algorithmic_bytes": fb, "ms": t_fwd}
+    roof_fwd["frac"] = roof_fwd["achieved"] / hbm
+    step_roof = {"achieved": (fb + bb) / (ms * 1e-3) / 1e9, "peak": hbm, "unit": "GB/s"}
+    step_roof["frac"] = step_roof["achieved"] / hbm
+
+    # --- end to end through the public API: pinned host inputs -> device, fwd+bwd,
+    # outputs and gradients -> pinned host
+    pin = {k: torch.from_numpy(v).pin_memory() for k, v in h.items()}
+    outs_host = None
+    h2d = sum(v.numel() * v.element_size() for v in pin.values())
+    ee0, ee1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    d2h = 0
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ee0.record(stream)
+    for _ in range(args.e2e_steps):
+        dv = {k: v.to(dev, non_blocking=True) for k, v in pin.items()}
+        for k in ("u", "delta", "z", "A", "B", "C", "D"):
+            dv[k].requires_grad_(True)
+        out = step(dv)
+        res = [out.detach()] + [dv[k].grad for k in ("u", "delta", "z", "A", "B", "C", "D")]
+        if outs_host is None:
+            outs_host = [torch.empty(r.shape, dtype=r.dtype, pin_memory=True) for r in res]
+            d2h = sum(r.numel() * r.element_size() for r in res)
+        for hbuf, r in zip(outs_host, res):
+            hbuf.copy_(r, non_blocking=True)
+    ee1.record(stream)
+    torch.cuda.synchronize()
+    ems = ee0.elapsed_time(ee1) / args.e2e_steps
+    if world > 1:
+        mt = torch.tensor([ems], device=dev)
+        dist.all_reduce(mt, op=dist.ReduceOp.MAX)
+        ems = float(mt.item())
+
+    line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": max(3, args.warmup), "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": config,
+            "roofline": roof_bwd, "roofline_fwd": roof_fwd, "roofline_step": step_roof,
+            "e2e": {"value": units * world / (ems * 1e-3), "unit": UNIT, "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "ms_per_step": ems},
+            "gpu_launches": launches_per_step * args.steps,
+            "clocks": clk.summary(), "library": lib.ssm_version().decode()}
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        v, secs, sample = run_cpu_sample(seqlen=256)
+        line["cpu_baseline"] = {"value": v, "unit": UNIT, "cores": cpu_threads(), "kind": "port",
+                                "sample": sample, "seconds": secs}
+    if rank == 0:
+        print(json.dumps(line))
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

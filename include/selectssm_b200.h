@@ -1,0 +1,181 @@
+/*
+ * selectssm_b200 -- C ABI of the B200 (sm_100a) selective-scan hot path.
+ *
+ * The reference (ihh/selectssm) is JAX/Flax.  Its hot path is a set of Python
+ * functions traced under jit; the FFI a JAX maintainer would bind for it is an
+ * XLA custom call (jax.ffi) per function.  Each entry point below is the plain
+ * C function such a custom-call handler wraps (see INTEGRATION.md for the
+ * handler shim and for the ctypes binding the tests use):
+ *
+ *   ssm_fwd        replaces ssm_chunked_scan / ssm_recursive_scan / ssm_scan
+ *                  forward (src/selectssm/selectssm.py:37-109,
+ *                  src/selectssm/ssmrecscan.py:36-88) together with the
+ *                  softplus(dt) of selectssm.py:210, the D skip of :238, the
+ *                  reverse/complement unflip of :230-231 and the gate of
+ *                  BidirectionalMamba (selectssm.py:335-338).
+ *   ssm_bwd        replaces the custom-VJP backward ssm_scan_backward
+ *                  (src/selectssm/ssmrecscan.py:111-181) and JAX autodiff of
+ *                  the chunked/recursive selectors, the softplus, skip and gate.
+ *   ssm_fwd_bidir / ssm_bwd_bidir
+ *                  both SelectiveSSM directions of BidirectionalMamba
+ *                  (selectssm.py:324-338) in one launch each.
+ *   ssm_conv1d_act_fwd / ssm_conv1d_act_bwd
+ *                  the flip + causal depthwise nn.Conv + activation preamble
+ *                  (selectssm.py:167-187) and its gradient.
+ *
+ * Conventions
+ *   - Layout is the reference's channels-last: activations (batch, seqlen, dim),
+ *     B/C (batch, seqlen, dstate), A (dim, dstate), D/delta_bias (dim).
+ *   - All pointers are device pointers owned by the caller.  Every call is
+ *     asynchronous on the given stream; nothing synchronises the host.
+ *   - Errors mirror the reference: shapes it rejects with ValueError return
+ *     SSM_ERR_SHAPE.  ssm_strerror() gives a message.
+ *   - Scratch memory is caller-provided (ssm_workspace_bytes()).
+ */
+#ifndef SELECTSSM_B200_H_
+#define SELECTSSM_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define SSM_API __attribute__((visibility("default")))
+#else
+#define SSM_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* ssm_stream_t; /* == cudaStream_t */
+
+enum ssm_status {
+  SSM_OK = 0,
+  SSM_ERR_SHAPE = 1,            /* sizes the reference rejects or this build does not support */
+  SSM_ERR_DTYPE = 2,            /* unsupported dtype code */
+  SSM_ERR_LAUNCH = 3,           /* CUDA launch / driver error */
+  SSM_ERR_TIMEOUT = 4,          /* a bounded device-side wait gave up (status word) */
+  SSM_ERR_NULL = 5,             /* a required pointer is NULL */
+  SSM_ERR_ALIGN = 6,            /* pointer / stride alignment not met (16 bytes) */
+  SSM_ERR_WORKSPACE = 7         /* workspace missing or too small */
+};
+
+enum ssm_dtype { SSM_F32 = 0, SSM_BF16 = 1 };
+
+enum ssm_flags {
+  SSM_DELTA_SOFTPLUS = 1 << 0,  /* dt = softplus(delta + delta_bias)  (selectssm.py:210) */
+  SSM_REVERSE = 1 << 1,         /* SelectiveSSM.reverse: output / z / skip in the unflipped frame */
+  SSM_COMPLEMENT = 1 << 2,      /* SelectiveSSM.complement: the flip also reverses channels */
+  SSM_ALIGNED_SKIP = 1 << 3     /* opt-in: skip term flipped with y (the reference adds the
+                                   flipped-frame u unflipped, selectssm.py:231 then :238) */
+};
+
+enum ssm_act { SSM_ACT_NONE = 0, SSM_ACT_SILU = 1, SSM_ACT_GELU = 2, SSM_ACT_RELU = 3 };
+
+/* Scan chunk (forward checkpoint) length in steps.  The forward writes the
+ * state h (fp32, dstate values per channel) after every SSM_CHUNK steps; the
+ * backward restarts from those states. */
+#define SSM_CHUNK 16
+
+typedef struct ssm_params {
+  int32_t batch, seqlen, dim, dstate;   /* B, L, D, N (N must be 16) */
+  int32_t dtype;                        /* u, delta, z, out, dout, du, ddelta, dz */
+  int32_t bc_dtype;                     /* B, C, dB, dC */
+  int32_t flags;                        /* ssm_flags */
+  int32_t gate_act;                     /* ssm_act applied to z; ignored when z == NULL */
+  /* Row strides in elements between consecutive (b, l) rows; 0 means dense
+   * (dim for activations, dstate for B/C).  They let the caller pass slices of a
+   * wider buffer (in_proj splits, the concatenated fwd/rev output). */
+  int64_t z_stride;                     /* z and dz */
+  int64_t out_stride;                   /* out and dout */
+  int64_t bc_stride;                    /* B, C, dB, dC */
+
+  /* ---- forward inputs (scan frame unless noted) ---- */
+  const void* u;                        /* (B,L,D) scan input x (post-conv activation)   */
+  const void* delta;                    /* (B,L,D) dt before bias / softplus             */
+  const float* A;                       /* (D,N)   A = -exp(A_log)                        */
+  const void* Bm;                       /* (B,L,N)                                       */
+  const void* Cm;                       /* (B,L,N)                                       */
+  const float* D;                       /* (D)     skip weight, NULL: no skip            */
+  const float* delta_bias;              /* (D)     NULL: no bias                         */
+  const void* z;                        /* (B,L,D) gate input, output frame; NULL: no gate */
+  /* ---- forward outputs ---- */
+  void* out;                            /* (B,L,D) output frame                          */
+  float* states;                        /* (B, ceil(L/16), D, N) fp32 state after each chunk;
+                                           written by ssm_fwd, read by ssm_bwd            */
+  /* ---- backward ---- */
+  const void* dout;                     /* (B,L,D) output frame                          */
+  void* du;                             /* (B,L,D)                                       */
+  void* ddelta;                         /* (B,L,D) grad w.r.t. delta (pre-bias/softplus) */
+  float* dA;                            /* (D,N)                                         */
+  void* dB;                             /* (B,L,N)                                       */
+  void* dC;                             /* (B,L,N)                                       */
+  float* dD;                            /* (D)     required when D != NULL               */
+  float* ddelta_bias;                   /* (D)     required when delta_bias != NULL      */
+  void* dz;                             /* (B,L,D) required when z != NULL               */
+  /* ---- scratch ---- */
+  void* workspace;                      /* ssm_workspace_bytes() bytes, 256-byte aligned */
+  size_t workspace_bytes;
+  int32_t* status;                      /* optional device word: nonzero after a device-side
+                                           failure (bounded wait gave up)                 */
+} ssm_params_t;
+
+/* Bytes of scratch the backward needs for these params (the forward needs none). */
+SSM_API size_t ssm_workspace_bytes(const ssm_params_t* p);
+/* Number of floats of p->states: B * ceil(L/16) * D * N. */
+SSM_API size_t ssm_states_elems(const ssm_params_t* p);
+
+/* Forward (see top of file).  Writes out and states. */
+SSM_API int ssm_fwd(const ssm_params_t* p, ssm_stream_t stream);
+/* Backward.  Needs the states written by ssm_fwd on the same inputs.  Writes
+ * du, ddelta, dA, dB, dC and, when present, dD, ddelta_bias, dz (overwritten). */
+SSM_API int ssm_bwd(const ssm_params_t* p, ssm_stream_t stream);
+
+/* Both directions of a BidirectionalMamba block in one launch each.  fwd and
+ * rev are complete parameter sets (rev normally has SSM_REVERSE, and
+ * SSM_COMPLEMENT when complement=True); they may share z (tie_gate) and write
+ * disjoint channel ranges of one output (concatenate_fwd_rev).  When z is shared,
+ * dz must not be: the two directions' dz are separate buffers for the caller to add.
+ * Shapes and dtypes of the two sets must match; workspace must hold
+ * ssm_workspace_bytes(fwd) + ssm_workspace_bytes(rev) in fwd->workspace.       */
+SSM_API int ssm_fwd_bidir(const ssm_params_t* fwd, const ssm_params_t* rev, ssm_stream_t stream);
+SSM_API int ssm_bwd_bidir(const ssm_params_t* fwd, const ssm_params_t* rev, ssm_stream_t stream);
+
+/* ---- causal depthwise conv1d + activation (selectssm.py:167-187) ----
+ * u[b,t,c] = act( sum_{k<K} w[k,c] * xt[b, t+k-(K-1), c] ),
+ * xt = x, or x flipped in L (and in channels with SSM_COMPLEMENT) with
+ * SSM_REVERSE.  x is (B,L,D) in its own frame; u is in the scan frame.
+ * w is Flax's shift_conv kernel (K,1,D) viewed as (K,D), fp32. */
+typedef struct ssm_conv_params {
+  int32_t batch, seqlen, dim, width;    /* B, L, D, K (1 <= K <= 8) */
+  int32_t dtype;                        /* x, u, du, dx */
+  int32_t flags;                        /* SSM_REVERSE | SSM_COMPLEMENT */
+  int32_t act;                          /* ssm_act */
+  int64_t x_stride;                     /* row stride of x and dx in elements, 0 = dim */
+  const void* x;
+  const float* w;
+  void* u;                              /* forward output (B,L,D) dense */
+  const void* du;                       /* backward input (B,L,D) dense */
+  void* dx;                             /* backward output, x's layout */
+  float* dw;                            /* backward output (K,D) */
+  void* workspace;
+  size_t workspace_bytes;
+} ssm_conv_params_t;
+
+SSM_API size_t ssm_conv1d_workspace_bytes(const ssm_conv_params_t* p);
+SSM_API int ssm_conv1d_act_fwd(const ssm_conv_params_t* p, ssm_stream_t stream);
+SSM_API int ssm_conv1d_act_bwd(const ssm_conv_params_t* p, ssm_stream_t stream);
+
+/* Message for a status code (static storage). */
+SSM_API const char* ssm_strerror(int status);
+/* Detail (CUDA error string and call site) of the most recent SSM_ERR_LAUNCH
+ * returned on the calling host thread; "" if none. */
+SSM_API const char* ssm_last_error(void);
+/* Library version string. */
+SSM_API const char* ssm_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* SELECTSSM_B200_H_ */

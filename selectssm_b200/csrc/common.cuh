@@ -1,0 +1,176 @@
+// Device helpers shared by the selective-scan kernels (sm_100a).
+//
+// Everything here is hand-written PTX for data movement (mbarrier, TMA tensor
+// loads) and for the hardware special-function instructions (ex2/lg2/rcp).
+#pragma once
+
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+namespace ssm {
+
+constexpr int kChunk = 16;        // steps per chunk == checkpoint spacing
+constexpr int kN = 16;            // state size supported by this build
+constexpr int kNL = 4;            // states owned by one lane
+constexpr int kLanesPerCh = kN / kNL;          // 4 lanes share one channel
+constexpr int kChPerWarp = 32 / kLanesPerCh;   // 8 channels per warp
+constexpr int kWarps = 4;                      // warps per CTA
+constexpr int kTileCh = kChPerWarp * kWarps;   // 32 channels per CTA
+constexpr int kThreads = 32 * kWarps;
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+// Upper bound on polls of an mbarrier before a kernel gives up (each poll of
+// try_wait suspends for a hardware-defined time, so this is seconds, not a
+// tight loop).
+constexpr uint32_t kSpinLimit = 1u << 24;
+
+// error codes written to the optional status word
+constexpr int kStatusTimeout = 4;
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// ---------------------------------------------------------------- mbarrier
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait: returns false if the barrier did not complete within kSpinLimit polls.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
+  for (uint32_t i = 0; i < kSpinLimit; ++i)
+    if (mbar_try_wait(bar, parity)) return true;
+  return false;
+}
+
+// ---------------------------------------------------------------- TMA
+// 3-D tiled tensor load (no multicast): box lands at `dst`, completion counted
+// on `bar` in bytes.  Coordinates are (channel, step, batch); the channel
+// coordinate times the element size must be a multiple of 16 bytes.
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1,
+                                            int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// ---------------------------------------------------------------- math
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float lg2(float x) {
+  float y;
+  asm("lg2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float rcp(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// softplus(x) = log(1 + e^x).  For x < -3 the Taylor series of log1p(e)
+// (e = e^x < 0.05; six terms, relative truncation below 3e-9) avoids the
+// cancellation of log(1 + small); for x > 20 softplus(x) == x in fp32.
+__device__ __forceinline__ float softplus_f(float x) {
+  if (x > 20.f) return x;
+  const float e = ex2(x * kLog2e);
+  if (x < -3.f) {
+    const float p = 0.2f - e * (1.f / 6.f);
+    return e * (1.f - e * (0.5f - e * (1.f / 3.f - e * (0.25f - e * p))));
+  }
+  return lg2(1.f + e) * kLn2;
+}
+// logistic sigmoid
+__device__ __forceinline__ float sigmoid_f(float x) { return rcp(1.f + ex2(-x * kLog2e)); }
+
+// tanh from the exponential: tanh(x) = 1 - 2 / (1 + e^{2x}) (absolute error
+// ~1e-7, which is what the gelu gate needs).
+__device__ __forceinline__ float tanh_f(float x) {
+  x = fminf(fmaxf(x, -15.f), 15.f);
+  return 1.f - 2.f * rcp(1.f + ex2(2.f * kLog2e * x));
+}
+
+constexpr float kGeluC = 0.7978845608028654f;  // sqrt(2/pi)
+
+// activation and its derivative; act is an ssm_act code
+__device__ __forceinline__ float act_f(float x, int act) {
+  switch (act) {
+    case 1: return x * sigmoid_f(x);
+    case 2: return 0.5f * x * (1.f + tanh_f(kGeluC * (x + 0.044715f * x * x * x)));
+    case 3: return fmaxf(x, 0.f);
+    default: return x;
+  }
+}
+__device__ __forceinline__ float act_grad_f(float x, int act) {
+  switch (act) {
+    case 1: {
+      const float s = sigmoid_f(x);
+      return s * (1.f + x * (1.f - s));
+    }
+    case 2: {
+      const float t = tanh_f(kGeluC * (x + 0.044715f * x * x * x));
+      const float di = kGeluC * (1.f + 3.f * 0.044715f * x * x);
+      return 0.5f * (1.f + t) + 0.5f * x * (1.f - t * t) * di;
+    }
+    case 3: return x > 0.f ? 1.f : 0.f;
+    default: return 1.f;
+  }
+}
+
+// ---------------------------------------------------------------- dtype helpers
+template <typename T> struct Cvt;
+template <> struct Cvt<float> {
+  __device__ __forceinline__ static float to_f(float v) { return v; }
+  __device__ __forceinline__ static float from_f(float v) { return v; }
+};
+template <> struct Cvt<__nv_bfloat16> {
+  __device__ __forceinline__ static float to_f(__nv_bfloat16 v) { return __bfloat162float(v); }
+  __device__ __forceinline__ static __nv_bfloat16 from_f(float v) { return __float2bfloat16_rn(v); }
+};
+template <typename T> __device__ __forceinline__ float ld_f(const T* p) { return Cvt<T>::to_f(*p); }
+
+// four consecutive values (16-byte aligned for float, 8-byte for bf16)
+__device__ __forceinline__ float4 ld4(const float* p) { return *reinterpret_cast<const float4*>(p); }
+__device__ __forceinline__ float4 ld4(const __nv_bfloat16* p) {
+  const uint2 r = *reinterpret_cast<const uint2*>(p);
+  __nv_bfloat162 a = *reinterpret_cast<const __nv_bfloat162*>(&r.x);
+  __nv_bfloat162 b = *reinterpret_cast<const __nv_bfloat162*>(&r.y);
+  const float2 fa = __bfloat1622float2(a), fb = __bfloat1622float2(b);
+  return make_float4(fa.x, fa.y, fb.x, fb.y);
+}
+
+__device__ __forceinline__ void report(int32_t* status, int code) {
+  if (status) atomicExch(status, code);
+}
+
+}  // namespace ssm

@@ -1,0 +1,482 @@
+// C-ABI entry points for the selective scan (forward, backward, bidirectional),
+// their argument checks, TMA descriptor set-up and launch sequences.
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "scan_kernels.cuh"
+
+namespace ssm {
+
+// Detail of the most recent SSM_ERR_LAUNCH on this host thread (diagnostics only).
+thread_local char g_last_error[256] = "";
+
+int launch_error(const char* where, cudaError_t e) {
+  snprintf(g_last_error, sizeof(g_last_error), "%s: %s", where, cudaGetErrorString(e));
+  return SSM_ERR_LAUNCH;
+}
+// Makes the device that owns `ptr` current for this library's runtime on the
+// calling thread (and its primary context current for driver calls such as
+// cuTensorMapEncodeTiled).  Callers may run on any host thread (e.g. an autograd
+// worker) and any device.
+int bind_device(const void* ptr) {
+  cudaPointerAttributes a;
+  cudaError_t e = cudaPointerGetAttributes(&a, ptr);
+  if (e != cudaSuccess) return launch_error("cudaPointerGetAttributes", e);
+  if (a.type != cudaMemoryTypeDevice && a.type != cudaMemoryTypeManaged) {
+    snprintf(g_last_error, sizeof(g_last_error), "pointer %p is not device memory", ptr);
+    return SSM_ERR_LAUNCH;
+  }
+  e = cudaSetDevice(a.device);
+  if (e != cudaSuccess) return launch_error("cudaSetDevice", e);
+  return SSM_OK;
+}
+
+#define SSM_CUDA_CHECK(call, where)        \
+  do {                                     \
+    cudaError_t e_ = (call);               \
+    if (e_ != cudaSuccess) return launch_error(where, e_); \
+  } while (0)
+
+// ---------------------------------------------------------------- small kernels
+// Zeroes `rows` rows of 16 floats spaced `stride` floats apart.
+__global__ void zero_rows16_kernel(float* p, int64_t rows, int64_t stride) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;  // one float4 per thread
+  if (i >= rows * 4) return;
+  const int64_t r = i >> 2;
+  reinterpret_cast<float4*>(p + r * stride)[i & 3] = make_float4(0.f, 0.f, 0.f, 0.f);
+}
+
+template <typename TBC>
+__global__ void finalize_kernel(FinalizeDir f) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t nDN = (int64_t)f.Dm * kN;
+  if (i < nDN) {  // dA: sum over batch rows in order
+    float s = 0.f;
+    for (int b = 0; b < f.batch; ++b) s += f.dA_part[(int64_t)b * nDN + i];
+    f.dA[i] = s;
+  }
+  if (i < f.Dm) {
+    if (f.dD) {
+      float s = 0.f;
+      for (int b = 0; b < f.batch; ++b) s += f.dD_part[(int64_t)b * f.Dm + i];
+      f.dD[i] = s;
+    }
+    if (f.dbias) {
+      float s = 0.f;
+      for (int b = 0; b < f.batch; ++b) s += f.db_part[(int64_t)b * f.Dm + i];
+      f.dbias[i] = s;
+    }
+  }
+  if (f.convert_bc) {
+    const int64_t nBC = (int64_t)f.batch * f.L * kN;
+    for (int64_t e = i; e < nBC; e += (int64_t)gridDim.x * blockDim.x) {
+      const int64_t r = e / kN, n = e % kN;
+      reinterpret_cast<TBC*>(f.dB)[r * f.bc_stride + n] = Cvt<TBC>::from_f(f.dB_acc[e]);
+      reinterpret_cast<TBC*>(f.dC)[r * f.bc_stride + n] = Cvt<TBC>::from_f(f.dC_acc[e]);
+    }
+  }
+}
+
+// ---------------------------------------------------------------- TMA descriptors
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {  // resolved once, read-only afterwards
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// 3-D tiled map over (d0 innermost, d1, d2) with row strides in bytes.
+static bool make_map(CUtensorMap* m, const void* base, bool bf16, uint64_t d0, uint64_t d1, uint64_t d2,
+                     uint64_t stride1_bytes, uint64_t stride2_bytes, uint32_t box0, uint32_t box1) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) {
+    snprintf(g_last_error, sizeof(g_last_error), "cuTensorMapEncodeTiled not available from the driver");
+    return false;
+  }
+  const cuuint64_t dims[3] = {d0, d1, d2};
+  const cuuint64_t strides[2] = {stride1_bytes, stride2_bytes};
+  const cuuint32_t box[3] = {box0, box1, 1};
+  const cuuint32_t es[3] = {1, 1, 1};
+  const CUresult r = fn(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3,
+                        const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    snprintf(g_last_error, sizeof(g_last_error),
+             "cuTensorMapEncodeTiled error %d: base %p dims {%llu,%llu,%llu} strides {%llu,%llu} box {%u,%u}",
+             (int)r, base, (unsigned long long)d0, (unsigned long long)d1, (unsigned long long)d2,
+             (unsigned long long)stride1_bytes, (unsigned long long)stride2_bytes, box0, box1);
+  return r == CUDA_SUCCESS;
+}
+
+// ---------------------------------------------------------------- validation
+static inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+struct Geo {
+  int B, L, Dm, nblk;
+  int es, esbc;  // element sizes
+  bool bf16, bcbf16;
+  int64_t zs, os, bs;  // row strides in elements
+};
+
+static int check_common(const ssm_params_t* p, Geo* g) {
+  if (!p) return SSM_ERR_NULL;
+  if (p->batch < 0 || p->seqlen < 0 || p->dim < 0) return SSM_ERR_SHAPE;
+  if (p->dstate != kN) return SSM_ERR_SHAPE;
+  if (p->batch > 65535) return SSM_ERR_SHAPE;
+  if ((p->dtype != SSM_F32 && p->dtype != SSM_BF16) || (p->bc_dtype != SSM_F32 && p->bc_dtype != SSM_BF16))
+    return SSM_ERR_DTYPE;
+  if (p->gate_act < SSM_ACT_NONE || p->gate_act > SSM_ACT_RELU) return SSM_ERR_SHAPE;
+  g->B = p->batch;
+  g->L = p->seqlen;
+  g->Dm = p->dim;
+  g->nblk = (p->seqlen + kChunk - 1) / kChunk;
+  g->bf16 = p->dtype == SSM_BF16;
+  g->bcbf16 = p->bc_dtype == SSM_BF16;
+  g->es = g->bf16 ? 2 : 4;
+  g->esbc = g->bcbf16 ? 2 : 4;
+  g->zs = p->z_stride ? p->z_stride : p->dim;
+  g->os = p->out_stride ? p->out_stride : p->dim;
+  g->bs = p->bc_stride ? p->bc_stride : kN;
+  if (g->zs < p->dim || g->os < p->dim || g->bs < kN) return SSM_ERR_SHAPE;
+  // TMA: channel tiles (incl. the mirrored complement tile) start on 16-byte
+  // boundaries, and every row stride is a multiple of 16 bytes.
+  if (((int64_t)p->dim * g->es) % 16 || (g->zs * g->es) % 16 || (g->os * g->es) % 16 ||
+      (g->bs * g->esbc) % 16)
+    return SSM_ERR_ALIGN;
+  return SSM_OK;
+}
+
+// inputs shared by the forward and the backward
+static int check_inputs(const ssm_params_t* p, Geo* g) {
+  int st = check_common(p, g);
+  if (st) return st;
+  if ((int64_t)g->B * g->L * g->Dm == 0) return SSM_OK;
+  if (!p->u || !p->delta || !p->A || !p->Bm || !p->Cm || !p->states) return SSM_ERR_NULL;
+  if (!aligned16(p->u) || !aligned16(p->delta) || !aligned16(p->Bm) || !aligned16(p->Cm) ||
+      !aligned16(p->states) || !aligned16(p->A) || (p->z && !aligned16(p->z)))
+    return SSM_ERR_ALIGN;
+  return SSM_OK;
+}
+
+static int check_fwd(const ssm_params_t* p, Geo* g) {
+  int st = check_inputs(p, g);
+  if (st) return st;
+  if ((int64_t)g->B * g->L * g->Dm != 0 && !p->out) return SSM_ERR_NULL;
+  return SSM_OK;
+}
+
+static int check_bwd(const ssm_params_t* p, Geo* g) {
+  int st = check_inputs(p, g);
+  if (st) return st;
+  if (!p->dA || (p->D && !p->dD) || (p->delta_bias && !p->ddelta_bias)) return SSM_ERR_NULL;
+  if ((int64_t)g->B * g->L * g->Dm == 0) return SSM_OK;
+  if (!p->dout || !p->du || !p->ddelta || !p->dB || !p->dC || (p->z && !p->dz)) return SSM_ERR_NULL;
+  if (!aligned16(p->dout) || !aligned16(p->dB) || !aligned16(p->dC)) return SSM_ERR_ALIGN;
+  return SSM_OK;
+}
+
+static size_t round256(size_t x) { return (x + 255) & ~size_t(255); }
+
+static size_t bwd_ws_bytes(const Geo& g) {
+  size_t n = round256((size_t)g.B * g.Dm * kN * 4) + 2 * round256((size_t)g.B * g.Dm * 4);
+  if (g.bcbf16) n += 2 * round256((size_t)g.B * g.L * kN * 4);
+  return n;
+}
+
+// ---------------------------------------------------------------- forward launch
+static int fill_fwd_dir(const ssm_params_t* p, const Geo& g, FwdDir* d) {
+  const uint64_t es = g.es, eb = g.esbc;
+  bool ok = make_map(&d->tm_u, p->u, g.bf16, g.Dm, g.L, g.B, g.Dm * es, (uint64_t)g.L * g.Dm * es, kTileCh, kChunk);
+  ok = ok && make_map(&d->tm_delta, p->delta, g.bf16, g.Dm, g.L, g.B, g.Dm * es, (uint64_t)g.L * g.Dm * es,
+                      kTileCh, kChunk);
+  ok = ok && make_map(&d->tm_B, p->Bm, g.bcbf16, kN, g.L, g.B, g.bs * eb, (uint64_t)g.L * g.bs * eb, kN, kChunk);
+  ok = ok && make_map(&d->tm_C, p->Cm, g.bcbf16, kN, g.L, g.B, g.bs * eb, (uint64_t)g.L * g.bs * eb, kN, kChunk);
+  if (p->z)
+    ok = ok && make_map(&d->tm_z, p->z, g.bf16, g.Dm, g.L, g.B, g.zs * es, (uint64_t)g.L * g.zs * es, kTileCh,
+                        kChunk);
+  else
+    std::memset(&d->tm_z, 0, sizeof(d->tm_z));
+  if (!ok) return SSM_ERR_LAUNCH;  // detail recorded by make_map
+  d->A = p->A;
+  d->D = p->D;
+  d->bias = p->delta_bias;
+  d->out = p->out;
+  d->states = p->states;
+  d->status = p->status;
+  d->out_stride = g.os;
+  d->L = g.L;
+  d->Dm = g.Dm;
+  d->flags = p->flags;
+  d->gate_act = p->z ? p->gate_act : SSM_ACT_NONE;
+  d->has_z = p->z != nullptr;
+  return SSM_OK;
+}
+
+template <typename T, typename TBC>
+static int launch_fwd_t(const FwdLaunch& L, int ndir, const Geo& g, cudaStream_t s) {
+  using S = FwdSmem<T, TBC>;
+  auto kern = ssm_fwd_kernel<T, TBC>;
+  SSM_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kBytes),
+                 "cudaFuncSetAttribute(ssm_fwd_kernel)");
+  dim3 grid((g.Dm + kTileCh - 1) / kTileCh, g.B, ndir);
+  kern<<<grid, kThreads, S::kBytes, s>>>(L);
+  SSM_CUDA_CHECK(cudaGetLastError(), "launch ssm_fwd_kernel");
+  return SSM_OK;
+}
+
+static int launch_fwd(const FwdLaunch& L, int ndir, const Geo& g, cudaStream_t s) {
+  if (!g.bf16 && !g.bcbf16) return launch_fwd_t<float, float>(L, ndir, g, s);
+  if (!g.bf16 && g.bcbf16) return launch_fwd_t<float, __nv_bfloat16>(L, ndir, g, s);
+  if (g.bf16 && !g.bcbf16) return launch_fwd_t<__nv_bfloat16, float>(L, ndir, g, s);
+  return launch_fwd_t<__nv_bfloat16, __nv_bfloat16>(L, ndir, g, s);
+}
+
+// ---------------------------------------------------------------- backward launch
+struct BwdWs {
+  float *dA_part, *dD_part, *db_part, *dB_acc, *dC_acc;
+  int64_t acc_stride;
+};
+
+static void carve_ws(const ssm_params_t* p, const Geo& g, char* ws, BwdWs* w) {
+  w->dA_part = reinterpret_cast<float*>(ws);
+  ws += round256((size_t)g.B * g.Dm * kN * 4);
+  w->dD_part = reinterpret_cast<float*>(ws);
+  ws += round256((size_t)g.B * g.Dm * 4);
+  w->db_part = reinterpret_cast<float*>(ws);
+  ws += round256((size_t)g.B * g.Dm * 4);
+  if (g.bcbf16) {
+    w->dB_acc = reinterpret_cast<float*>(ws);
+    ws += round256((size_t)g.B * g.L * kN * 4);
+    w->dC_acc = reinterpret_cast<float*>(ws);
+    w->acc_stride = kN;
+  } else {
+    w->dB_acc = reinterpret_cast<float*>(p->dB);
+    w->dC_acc = reinterpret_cast<float*>(p->dC);
+    w->acc_stride = g.bs;
+  }
+}
+
+static int fill_bwd_dir(const ssm_params_t* p, const Geo& g, const BwdWs& w, BwdDir* d) {
+  const uint64_t es = g.es, eb = g.esbc;
+  bool ok = make_map(&d->tm_u, p->u, g.bf16, g.Dm, g.L, g.B, g.Dm * es, (uint64_t)g.L * g.Dm * es, kTileCh, kChunk);
+  ok = ok && make_map(&d->tm_delta, p->delta, g.bf16, g.Dm, g.L, g.B, g.Dm * es, (uint64_t)g.L * g.Dm * es,
+                      kTileCh, kChunk);
+  ok = ok && make_map(&d->tm_B, p->Bm, g.bcbf16, kN, g.L, g.B, g.bs * eb, (uint64_t)g.L * g.bs * eb, kN, kChunk);
+  ok = ok && make_map(&d->tm_C, p->Cm, g.bcbf16, kN, g.L, g.B, g.bs * eb, (uint64_t)g.L * g.bs * eb, kN, kChunk);
+  ok = ok && make_map(&d->tm_dout, p->dout, g.bf16, g.Dm, g.L, g.B, g.os * es, (uint64_t)g.L * g.os * es, kTileCh,
+                      kChunk);
+  if (p->z)
+    ok = ok && make_map(&d->tm_z, p->z, g.bf16, g.Dm, g.L, g.B, g.zs * es, (uint64_t)g.L * g.zs * es, kTileCh,
+                        kChunk);
+  else
+    std::memset(&d->tm_z, 0, sizeof(d->tm_z));
+  ok = ok && make_map(&d->tm_states, p->states, false, kN, g.Dm, (uint64_t)g.B * g.nblk, kN * 4,
+                      (uint64_t)g.Dm * kN * 4, kN, kTileCh);
+  if (!ok) return SSM_ERR_LAUNCH;  // detail recorded by make_map
+  d->A = p->A;
+  d->D = p->D;
+  d->bias = p->delta_bias;
+  d->du = p->du;
+  d->ddelta = p->ddelta;
+  d->dz = p->dz;
+  d->dB_acc = w.dB_acc;
+  d->dC_acc = w.dC_acc;
+  d->dA_part = w.dA_part;
+  d->dD_part = w.dD_part;
+  d->db_part = w.db_part;
+  d->status = p->status;
+  d->z_stride = g.zs;
+  d->acc_stride = w.acc_stride;
+  d->L = g.L;
+  d->Dm = g.Dm;
+  d->flags = p->flags;
+  d->gate_act = p->z ? p->gate_act : SSM_ACT_NONE;
+  d->has_z = p->z != nullptr;
+  return SSM_OK;
+}
+
+template <typename T, typename TBC>
+static int launch_bwd_t(const BwdLaunch& L, int ndir, const Geo& g, cudaStream_t s) {
+  using S = BwdSmem<T, TBC>;
+  auto kern = ssm_bwd_kernel<T, TBC>;
+  SSM_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kBytes),
+                 "cudaFuncSetAttribute(ssm_bwd_kernel)");
+  dim3 grid((g.Dm + kTileCh - 1) / kTileCh, g.B, ndir);
+  kern<<<grid, kThreads, S::kBytes, s>>>(L);
+  SSM_CUDA_CHECK(cudaGetLastError(), "launch ssm_bwd_kernel");
+  return SSM_OK;
+}
+
+static int launch_bwd(const BwdLaunch& L, int ndir, const Geo& g, cudaStream_t s) {
+  if (!g.bf16 && !g.bcbf16) return launch_bwd_t<float, float>(L, ndir, g, s);
+  if (!g.bf16 && g.bcbf16) return launch_bwd_t<float, __nv_bfloat16>(L, ndir, g, s);
+  if (g.bf16 && !g.bcbf16) return launch_bwd_t<__nv_bfloat16, float>(L, ndir, g, s);
+  return launch_bwd_t<__nv_bfloat16, __nv_bfloat16>(L, ndir, g, s);
+}
+
+static int launch_zero_acc(const Geo& g, const BwdWs& w, cudaStream_t s) {
+  const int64_t rows = (int64_t)g.B * g.L;
+  if (rows == 0) return SSM_OK;
+  const int64_t n = rows * 4;
+  const int threads = 256;
+  const unsigned blocks = (unsigned)((n + threads - 1) / threads);
+  zero_rows16_kernel<<<blocks, threads, 0, s>>>(w.dB_acc, rows, w.acc_stride);
+  zero_rows16_kernel<<<blocks, threads, 0, s>>>(w.dC_acc, rows, w.acc_stride);
+  SSM_CUDA_CHECK(cudaGetLastError(), "launch zero_rows16_kernel");
+  return SSM_OK;
+}
+
+static int launch_finalize(const ssm_params_t* p, const Geo& g, const BwdWs& w, cudaStream_t s) {
+  FinalizeDir f;
+  f.dA_part = w.dA_part;
+  f.dD_part = w.dD_part;
+  f.db_part = w.db_part;
+  f.dA = p->dA;
+  f.dD = p->D ? p->dD : nullptr;
+  f.dbias = p->delta_bias ? p->ddelta_bias : nullptr;
+  f.dB_acc = w.dB_acc;
+  f.dC_acc = w.dC_acc;
+  f.dB = p->dB;
+  f.dC = p->dC;
+  f.bc_stride = g.bs;
+  f.batch = g.B;
+  f.L = g.L;
+  f.Dm = g.Dm;
+  f.convert_bc = g.bcbf16 && (int64_t)g.B * g.L > 0;
+  const int threads = 256;
+  int64_t n = (int64_t)g.Dm * kN;
+  unsigned blocks = (unsigned)((n + threads - 1) / threads);
+  if (f.convert_bc) blocks = blocks < 1184 ? 1184 : blocks;
+  if (blocks == 0) return SSM_OK;
+  if (g.bcbf16)
+    finalize_kernel<__nv_bfloat16><<<blocks, threads, 0, s>>>(f);
+  else
+    finalize_kernel<float><<<blocks, threads, 0, s>>>(f);
+  SSM_CUDA_CHECK(cudaGetLastError(), "launch finalize_kernel");
+  return SSM_OK;
+}
+
+static bool same_geo(const Geo& a, const Geo& b) {
+  return a.B == b.B && a.L == b.L && a.Dm == b.Dm && a.bf16 == b.bf16 && a.bcbf16 == b.bcbf16;
+}
+
+}  // namespace ssm
+
+using namespace ssm;
+
+extern "C" {
+
+size_t ssm_states_elems(const ssm_params_t* p) {
+  if (!p || p->batch <= 0 || p->seqlen <= 0 || p->dim <= 0) return 0;
+  return (size_t)p->batch * ((p->seqlen + kChunk - 1) / kChunk) * p->dim * kN;
+}
+
+size_t ssm_workspace_bytes(const ssm_params_t* p) {
+  Geo g;
+  if (check_common(p, &g) != SSM_OK) return 0;
+  return bwd_ws_bytes(g);
+}
+
+int ssm_fwd(const ssm_params_t* p, ssm_stream_t stream) { return ssm_fwd_bidir(p, nullptr, stream); }
+
+int ssm_fwd_bidir(const ssm_params_t* fwd, const ssm_params_t* rev, ssm_stream_t stream) {
+  Geo g, g2;
+  int st = check_fwd(fwd, &g);
+  if (st) return st;
+  if (rev) {
+    st = check_fwd(rev, &g2);
+    if (st) return st;
+    if (!same_geo(g, g2)) return SSM_ERR_SHAPE;
+  }
+  if ((int64_t)g.B * g.L * g.Dm == 0) return SSM_OK;
+  st = bind_device(fwd->u);
+  if (st) return st;
+  FwdLaunch args;
+  std::memset(&args, 0, sizeof(args));
+  st = fill_fwd_dir(fwd, g, &args.dir[0]);
+  if (!st && rev) st = fill_fwd_dir(rev, g, &args.dir[1]);
+  if (st) return st;
+  return launch_fwd(args, rev ? 2 : 1, g, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int ssm_bwd(const ssm_params_t* p, ssm_stream_t stream) { return ssm_bwd_bidir(p, nullptr, stream); }
+
+int ssm_bwd_bidir(const ssm_params_t* fwd, const ssm_params_t* rev, ssm_stream_t stream) {
+  Geo g, g2;
+  int st = check_bwd(fwd, &g);
+  if (st) return st;
+  if (rev) {
+    st = check_bwd(rev, &g2);
+    if (st) return st;
+    if (!same_geo(g, g2)) return SSM_ERR_SHAPE;
+  }
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  st = bind_device((int64_t)g.B * g.L * g.Dm ? fwd->u : (const void*)fwd->dA);
+  if (st) return st;
+  const size_t need = bwd_ws_bytes(g) * (rev ? 2 : 1);
+  if (need && (!fwd->workspace || fwd->workspace_bytes < need)) return SSM_ERR_WORKSPACE;
+  if (reinterpret_cast<uintptr_t>(fwd->workspace) & 255u) return SSM_ERR_ALIGN;
+  BwdWs w[2];
+  carve_ws(fwd, g, static_cast<char*>(fwd->workspace), &w[0]);
+  if (rev) carve_ws(rev, g, static_cast<char*>(fwd->workspace) + bwd_ws_bytes(g), &w[1]);
+  const int ndir = rev ? 2 : 1;
+  const ssm_params_t* ps[2] = {fwd, rev};
+  if ((int64_t)g.B * g.L * g.Dm == 0) {
+    // nothing to scan: parameter gradients are zero
+    for (int d = 0; d < ndir; ++d) {
+      if (g.Dm == 0) continue;
+      SSM_CUDA_CHECK(cudaMemsetAsync(ps[d]->dA, 0, (size_t)g.Dm * kN * 4, s), "cudaMemsetAsync(dA)");
+      if (ps[d]->D) SSM_CUDA_CHECK(cudaMemsetAsync(ps[d]->dD, 0, (size_t)g.Dm * 4, s), "cudaMemsetAsync(dD)");
+      if (ps[d]->delta_bias)
+        SSM_CUDA_CHECK(cudaMemsetAsync(ps[d]->ddelta_bias, 0, (size_t)g.Dm * 4, s), "cudaMemsetAsync(dbias)");
+    }
+    return SSM_OK;
+  }
+  BwdLaunch args;
+  std::memset(&args, 0, sizeof(args));
+  for (int d = 0; d < ndir; ++d) {
+    st = fill_bwd_dir(ps[d], g, w[d], &args.dir[d]);
+    if (st) return st;
+    st = launch_zero_acc(g, w[d], s);
+    if (st) return st;
+  }
+  st = launch_bwd(args, ndir, g, s);
+  if (st) return st;
+  for (int d = 0; d < ndir; ++d) {
+    st = launch_finalize(ps[d], g, w[d], s);
+    if (st) return st;
+  }
+  return SSM_OK;
+}
+
+const char* ssm_strerror(int status) {
+  switch (status) {
+    case SSM_OK: return "ok";
+    case SSM_ERR_SHAPE: return "unsupported or inconsistent shape (dstate must be 16; batch <= 65535)";
+    case SSM_ERR_DTYPE: return "unsupported dtype code";
+    case SSM_ERR_LAUNCH: return "CUDA launch or driver error";
+    case SSM_ERR_TIMEOUT: return "a bounded device-side wait gave up";
+    case SSM_ERR_NULL: return "a required pointer is NULL";
+    case SSM_ERR_ALIGN: return "pointer or row stride not 16-byte aligned (dim*elem_size must be a multiple of 16)";
+    case SSM_ERR_WORKSPACE: return "workspace missing, too small or not 256-byte aligned";
+    default: return "unknown status";
+  }
+}
+
+const char* ssm_version(void) { return "selectssm_b200 0.1.0 (sm_100a)"; }
+
+const char* ssm_last_error(void) { return g_last_error; }
+
+}  // extern "C"

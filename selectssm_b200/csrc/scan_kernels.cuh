@@ -1,0 +1,598 @@
+// Selective-scan forward / backward kernels for B200 (sm_100a).
+//
+// Work decomposition (both kernels)
+//   CTA   = one batch row b  x  32 consecutive channels  x  the whole sequence.
+//   warp  = 8 channels; lane = (channel ch = lane/4, state quarter nq = lane%4)
+//           and owns the 4 states n = 4*nq .. 4*nq+3 of its channel in registers.
+//   time  = processed in chunks of 16 steps.  Per chunk one elected thread issues
+//           TMA tile loads (32 ch x 16 steps of u / delta / z / dout, 16 x 16 of
+//           B and C, the chunk-start state) into a ring of shared-memory stages
+//           completed on mbarriers, so HBM reads run STAGES-1 chunks ahead.
+//   Each lane computes the per-step scalars (softplus(dt), dt*x, gate) for 4 of
+//   the chunk's 16 steps, and shares them with its channel's other 3 lanes by
+//   warp shuffles; y = C.h is reduced over those 4 lanes by two xor-shuffles.
+//
+// Forward: h_t = exp(A dt_t) h_{t-1} + dt_t B_t x_t (ZOH for A, Euler for B,
+//   src/selectssm/selectssm.py:74-78), y_t = C_t.h_t (:90), then the D skip
+//   (:238), the reverse/complement unflip (:230-231) and the gate y*act(z)
+//   (:335-338).  The state after every chunk is written to `states` (fp32).
+// Backward: chunks are visited last to first.  A chunk restarts from the saved
+//   state, recomputes exp(A dt) and the states of its 16 steps into registers
+//   (each exponential is evaluated once), then runs the adjoint
+//   f_t = alpha_{t+1} f_{t+1} + C_t dy_t backwards and forms the leaf gradients
+//   of src/selectssm/ssmrecscan.py:150-161:
+//     dx_t = dt_t sum_n f B_t,  dA += dt_t f alpha_t h_{t-1},  dB_t = sum_d dt_t x_t f,
+//     dC_t = sum_d dy_t h_t,    ddt_t = sum_n f (A alpha_t h_{t-1} + B_t x_t).
+//   dB/dC are reduced over the warp's 8 channels by a shuffle reduce-scatter,
+//   over the CTA's 4 warps in shared memory, and over channel tiles with one
+//   16-byte atomic add per thread per chunk.  dA/dD/d(delta_bias) are written
+//   as per-batch-row partials and summed in a fixed order by a finalize kernel.
+#pragma once
+
+#include "common.cuh"
+#include "../../include/selectssm_b200.h"
+
+namespace ssm {
+
+constexpr int kFwdStages = 4;
+constexpr int kBwdStages = 3;
+constexpr unsigned kFull = 0xffffffffu;
+
+// ---------------------------------------------------------------- arguments
+struct FwdDir {
+  CUtensorMap tm_u, tm_delta, tm_B, tm_C, tm_z;  // 64-byte aligned members first
+  const float* A;
+  const float* D;
+  const float* bias;
+  void* out;
+  float* states;
+  int32_t* status;
+  int64_t out_stride;
+  int L, Dm, flags, gate_act, has_z;
+};
+struct FwdLaunch {
+  FwdDir dir[2];
+};
+
+struct BwdDir {
+  CUtensorMap tm_u, tm_delta, tm_B, tm_C, tm_z, tm_dout, tm_states;
+  const float* A;
+  const float* D;
+  const float* bias;
+  void* du;
+  void* ddelta;
+  void* dz;
+  float* dB_acc;   // fp32 accumulation target for dB (row stride acc_stride)
+  float* dC_acc;
+  float* dA_part;  // (B, D, 16)
+  float* dD_part;  // (B, D)
+  float* db_part;  // (B, D)
+  int32_t* status;
+  int64_t z_stride, acc_stride;
+  int L, Dm, flags, gate_act, has_z;
+};
+struct BwdLaunch {
+  BwdDir dir[2];
+};
+
+template <typename T>
+__device__ __forceinline__ void st_act(T* p, float v) {
+  *p = Cvt<T>::from_f(v);
+}
+
+// ---------------------------------------------------------------- forward
+template <typename T, typename TBC>
+struct FwdSmem {
+  static constexpr int kAct = kChunk * kTileCh * (int)sizeof(T);   // one 16x32 activation tile
+  static constexpr int kBC = kChunk * kN * (int)sizeof(TBC);        // one 16x16 B or C tile
+  static constexpr int kOffU = 0, kOffDelta = kAct, kOffZ = 2 * kAct, kOffUo = 3 * kAct;
+  static constexpr int kOffB = 4 * kAct, kOffC = 4 * kAct + kBC;
+  static constexpr int kStage = 4 * kAct + 2 * kBC;
+  static constexpr int kBars = kStage * kFwdStages;
+  static constexpr int kBytes = kBars + 8 * kFwdStages;
+};
+
+template <typename T, typename TBC>
+__global__ void __launch_bounds__(kThreads, 3) ssm_fwd_kernel(const __grid_constant__ FwdLaunch P) {
+  using S = FwdSmem<T, TBC>;
+  const FwdDir& a = P.dir[blockIdx.z];
+  extern __shared__ __align__(1024) unsigned char smem[];
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::kBars);
+
+  const int b = blockIdx.y;
+  const int c0 = blockIdx.x * kTileCh;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int ch = lane >> 2, nq = lane & 3;
+  const int cl = warp * kChPerWarp + ch;
+  const int c = c0 + cl;
+  const int L = a.L, Dm = a.Dm;
+  if (c0 >= Dm) return;  // grid is sized for the larger direction
+  const bool rev = (a.flags & SSM_REVERSE) != 0;
+  const bool comp = rev && (a.flags & SSM_COMPLEMENT);
+  const bool aligned = (a.flags & SSM_ALIGNED_SKIP) != 0;
+  const bool softplus = (a.flags & SSM_DELTA_SOFTPLUS) != 0;
+  const bool has_z = a.has_z != 0, has_D = a.D != nullptr;
+  const bool need_uo = has_D && rev && !aligned;
+  const int nblk = (L + kChunk - 1) / kChunk;
+  const bool cvalid = c < Dm;
+  const int co = comp ? Dm - 1 - c : c;                 // output-frame channel
+  const int oc0 = comp ? Dm - kTileCh - c0 : c0;        // output-frame tile start
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kFwdStages; ++s) mbar_init(&bars[s], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  const uint32_t tx = 2 * S::kAct + 2 * S::kBC + (has_z ? S::kAct : 0) + (need_uo ? S::kAct : 0);
+  auto issue = [&](int j) {
+    unsigned char* st = smem + (j % kFwdStages) * S::kStage;
+    uint64_t* bar = &bars[j % kFwdStages];
+    const int t0 = j * kChunk;
+    const int ot0 = rev ? L - kChunk - t0 : t0;
+    mbar_arrive_expect_tx(bar, tx);
+    tma_load_3d(st + S::kOffU, &a.tm_u, bar, c0, t0, b);
+    tma_load_3d(st + S::kOffDelta, &a.tm_delta, bar, c0, t0, b);
+    tma_load_3d(st + S::kOffB, &a.tm_B, bar, 0, t0, b);
+    tma_load_3d(st + S::kOffC, &a.tm_C, bar, 0, t0, b);
+    if (has_z) tma_load_3d(st + S::kOffZ, &a.tm_z, bar, oc0, ot0, b);
+    if (need_uo) tma_load_3d(st + S::kOffUo, &a.tm_u, bar, oc0, ot0, b);
+  };
+  if (threadIdx.x == 0) {
+    const int npre = nblk < kFwdStages ? nblk : kFwdStages;
+    for (int j = 0; j < npre; ++j) issue(j);
+  }
+
+  // per-lane constants
+  float A2[kNL];
+#pragma unroll
+  for (int k = 0; k < kNL; ++k) A2[k] = cvalid ? a.A[(size_t)c * kN + nq * kNL + k] * kLog2e : 0.f;
+  const float bias = (a.bias && cvalid) ? a.bias[c] : 0.f;
+  const float Dsk = (has_D && cvalid) ? a.D[aligned ? c : co] : 0.f;
+  float h[kNL] = {0.f, 0.f, 0.f, 0.f};
+  T* out = reinterpret_cast<T*>(a.out);
+
+  for (int j = 0; j < nblk; ++j) {
+    const int s = j % kFwdStages;
+    const bool ok = mbar_wait_bounded(&bars[s], (j / kFwdStages) & 1);
+    if (!__syncthreads_and(ok)) {
+      if (threadIdx.x == 0) report(a.status, kStatusTimeout);
+      return;
+    }
+    const unsigned char* st = smem + s * S::kStage;
+    const T* su = reinterpret_cast<const T*>(st + S::kOffU);
+    const T* sd = reinterpret_cast<const T*>(st + S::kOffDelta);
+    const T* sz = reinterpret_cast<const T*>(st + S::kOffZ);
+    const T* suo = reinterpret_cast<const T*>(st + S::kOffUo);
+    const TBC* sB = reinterpret_cast<const TBC*>(st + S::kOffB);
+    const TBC* sC = reinterpret_cast<const TBC*>(st + S::kOffC);
+
+    // per-step scalars for this lane's 4 steps (tl = nq + 4i)
+    float dtv[4], dtx[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int tl = nq + 4 * i;
+      const bool valid = j * kChunk + tl < L;
+      const float x = ld_f(su + tl * kTileCh + cl);
+      const float dr = ld_f(sd + tl * kTileCh + cl) + bias;
+      float dt = softplus ? softplus_f(dr) : dr;
+      dt = valid ? dt : 0.f;
+      dtv[i] = dt;
+      dtx[i] = valid ? dt * x : 0.f;
+    }
+
+    float yv[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int tl = 0; tl < kChunk; ++tl) {
+      const int src = (lane & ~3) | (tl & 3);
+      const float dt = __shfl_sync(kFull, dtv[tl >> 2], src);
+      const float dx = __shfl_sync(kFull, dtx[tl >> 2], src);
+      const float4 Bv = ld4(sB + tl * kN + nq * kNL);
+      const float4 Cv = ld4(sC + tl * kN + nq * kNL);
+      h[0] = fmaf(ex2(A2[0] * dt), h[0], Bv.x * dx);
+      h[1] = fmaf(ex2(A2[1] * dt), h[1], Bv.y * dx);
+      h[2] = fmaf(ex2(A2[2] * dt), h[2], Bv.z * dx);
+      h[3] = fmaf(ex2(A2[3] * dt), h[3], Bv.w * dx);
+      float yp = Cv.x * h[0] + Cv.y * h[1] + Cv.z * h[2] + Cv.w * h[3];
+      yp += __shfl_xor_sync(kFull, yp, 1);
+      yp += __shfl_xor_sync(kFull, yp, 2);
+      if ((tl & 3) == nq) yv[tl >> 2] = yp;
+    }
+
+    if (cvalid) {
+      float4* sp = reinterpret_cast<float4*>(a.states + (((size_t)b * nblk + j) * Dm + c) * kN + nq * kNL);
+      *sp = make_float4(h[0], h[1], h[2], h[3]);
+    }
+
+    // epilogue: skip, gate, store (lane's own 4 steps)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int tl = nq + 4 * i;
+      const int t = j * kChunk + tl;
+      if (t < L && cvalid) {
+        const int row = rev ? kChunk - 1 - tl : tl;
+        const int col = comp ? kTileCh - 1 - cl : cl;
+        const int l = rev ? L - 1 - t : t;
+        float y = yv[i];
+        if (has_D) {
+          const float xs = need_uo ? ld_f(suo + row * kTileCh + col) : ld_f(su + tl * kTileCh + cl);
+          y = fmaf(Dsk, xs, y);
+        }
+        if (has_z) y *= act_f(ld_f(sz + row * kTileCh + col), a.gate_act);
+        st_act(out + ((size_t)b * L + l) * a.out_stride + co, y);
+      }
+    }
+    __syncthreads();  // every warp is done with stage s
+    if (threadIdx.x == 0 && j + kFwdStages < nblk) {
+      fence_proxy_async_smem();
+      issue(j + kFwdStages);
+    }
+  }
+}
+
+// ---------------------------------------------------------------- backward
+constexpr int kHalf = kChunk / 2;
+
+// Compiler-only fence: keeps the scheduler from hoisting a whole unrolled
+// half-chunk of shared-memory loads ahead of use (which costs registers).
+__device__ __forceinline__ void sched_fence() { asm volatile("" ::: "memory"); }
+
+struct BwdLane {
+  int lane, nq, warp;
+  bool up4, up3, up2, has_z;
+};
+
+// Reduce-scatter of 4 values over the 8 channel lanes of a warp (lane bits 2..4):
+// returns the sum over the 8 channels of value k = 2*up4 + up3 (valid where !up2).
+__device__ __forceinline__ float reduce_scatter4(const BwdLane& ln, float v0, float v1, float v2, float v3) {
+  const float r0 = (ln.up4 ? v2 : v0) + __shfl_xor_sync(kFull, ln.up4 ? v0 : v2, 16);
+  const float r1 = (ln.up4 ? v3 : v1) + __shfl_xor_sync(kFull, ln.up4 ? v1 : v3, 16);
+  float q = (ln.up3 ? r1 : r0) + __shfl_xor_sync(kFull, ln.up3 ? r0 : r1, 8);
+  q += __shfl_xor_sync(kFull, q, 4);
+  return q;
+}
+
+// Forward recurrence over steps [T0, T0+kHalf) of the staged chunk, updating h.
+// STORE keeps alpha_t and alpha_t*h_{t-1} for the reverse sweep; SIDE also
+// forms y_t = C_t.h_t (owner lanes, for dz) and the dC_t = sum_d dy_t h_t partials.
+template <int T0, bool STORE, bool SIDE, typename TBC>
+__device__ __forceinline__ void bwd_forward_half(const BwdLane& ln, float (&h)[kNL], float (&al)[kHalf][kNL],
+                                                 float (&hq)[kHalf][kNL], float (&yv)[4], const float (&dtv)[4],
+                                                 const float (&dtx)[4], const float (&dys)[4],
+                                                 const float (&An)[kNL], const TBC* sB, const TBC* sC, float* red) {
+#pragma unroll
+  for (int tl = T0; tl < T0 + kHalf; ++tl) {
+    sched_fence();
+    const int src = (ln.lane & ~3) | (tl & 3);
+    const float dt = __shfl_sync(kFull, dtv[tl >> 2], src);
+    const float dx = __shfl_sync(kFull, dtx[tl >> 2], src);
+    const float dt2 = dt * kLog2e;
+    const float4 Bv = ld4(sB + tl * kN + ln.nq * kNL);
+    const float bv[4] = {Bv.x, Bv.y, Bv.z, Bv.w};
+#pragma unroll
+    for (int k = 0; k < kNL; ++k) {
+      const float a = ex2(An[k] * dt2);
+      const float q = a * h[k];
+      h[k] = fmaf(bv[k], dx, q);
+      if (STORE) {
+        al[tl - T0][k] = a;
+        hq[tl - T0][k] = q;
+      }
+    }
+    if (SIDE) {
+      const float dy = __shfl_sync(kFull, dys[tl >> 2], src);
+      const float4 Cv = ld4(sC + tl * kN + ln.nq * kNL);
+      if (ln.has_z) {
+        float yp = Cv.x * h[0] + Cv.y * h[1] + Cv.z * h[2] + Cv.w * h[3];
+        yp += __shfl_xor_sync(kFull, yp, 1);
+        yp += __shfl_xor_sync(kFull, yp, 2);
+        if ((tl & 3) == ln.nq) yv[tl >> 2] = yp;
+      }
+      const float s = reduce_scatter4(ln, dy * h[0], dy * h[1], dy * h[2], dy * h[3]);
+      if (!ln.up2) red[(ln.warp * kChunk + tl) * 32 + kN + ln.nq * kNL + (ln.up4 ? 2 : 0) + (ln.up3 ? 1 : 0)] = s;
+    }
+  }
+}
+
+// Adjoint sweep over steps T0+kHalf-1 .. T0: f_t = C_t dy_t + f_{t+1} alpha_{t+1}
+// (fa carries f alpha), with the leaf gradients of ssmrecscan.py:154-160.
+template <int T0, typename TBC, typename T>
+__device__ __forceinline__ void bwd_reverse_half(const BwdLane& ln, const float (&al)[kHalf][kNL],
+                                                 const float (&hq)[kHalf][kNL], float (&fa)[kNL], float (&dA)[kNL],
+                                                 const float (&dtv)[4], const float (&dtx)[4], const float (&dys)[4],
+                                                 const float (&An)[kNL], const TBC* sB, const TBC* sC,
+                                                 const T* su_col, float* red, float (&dxs)[4], float (&ddt)[4]) {
+#pragma unroll
+  for (int tl = T0 + kHalf - 1; tl >= T0; --tl) {
+    sched_fence();
+    const int src = (ln.lane & ~3) | (tl & 3);
+    const float dt = __shfl_sync(kFull, dtv[tl >> 2], src);
+    const float dx = __shfl_sync(kFull, dtx[tl >> 2], src);
+    const float dy = __shfl_sync(kFull, dys[tl >> 2], src);
+    const float4 Bv = ld4(sB + tl * kN + ln.nq * kNL);
+    const float4 Cv = ld4(sC + tl * kN + ln.nq * kNL);
+    const float bv[4] = {Bv.x, Bv.y, Bv.z, Bv.w};
+    const float cv[4] = {Cv.x, Cv.y, Cv.z, Cv.w};
+    float sAw = 0.f, sBf = 0.f, vB[kNL];
+#pragma unroll
+    for (int k = 0; k < kNL; ++k) {
+      const float f = fmaf(cv[k], dy, fa[k]);
+      const float w = f * hq[tl - T0][k];
+      dA[k] = fmaf(dt, w, dA[k]);
+      sAw = fmaf(An[k], w, sAw);
+      sBf = fmaf(bv[k], f, sBf);
+      vB[k] = dx * f;
+      fa[k] = f * al[tl - T0][k];
+    }
+    sAw += __shfl_xor_sync(kFull, sAw, 1);
+    sBf += __shfl_xor_sync(kFull, sBf, 1);
+    sAw += __shfl_xor_sync(kFull, sAw, 2);
+    sBf += __shfl_xor_sync(kFull, sBf, 2);
+    if ((tl & 3) == ln.nq) {
+      dxs[tl >> 2] = dt * sBf;
+      ddt[tl >> 2] = fmaf(ld_f(su_col + tl * kTileCh), sBf, sAw);  // x sum_n B f + sum_n A w
+    }
+    const float s = reduce_scatter4(ln, vB[0], vB[1], vB[2], vB[3]);
+    if (!ln.up2) red[(ln.warp * kChunk + tl) * 32 + ln.nq * kNL + (ln.up4 ? 2 : 0) + (ln.up3 ? 1 : 0)] = s;
+  }
+}
+
+template <typename T, typename TBC>
+struct BwdSmem {
+  static constexpr int kAct = kChunk * kTileCh * (int)sizeof(T);
+  static constexpr int kBC = kChunk * kN * (int)sizeof(TBC);
+  static constexpr int kSt = kTileCh * kN * 4;  // chunk-start state tile (fp32)
+  static constexpr int kOffU = 0, kOffDelta = kAct, kOffZo = 2 * kAct, kOffDo = 3 * kAct, kOffUo = 4 * kAct,
+                       kOffZs = 5 * kAct, kOffDs = 6 * kAct;
+  static constexpr int kOffB = 7 * kAct, kOffC = 7 * kAct + kBC, kOffS = 7 * kAct + 2 * kBC;
+  static constexpr int kStage = 7 * kAct + 2 * kBC + kSt;
+  static constexpr int kRed = kWarps * kChunk * 32 * 4;  // one dB/dC partial buffer
+  static constexpr int kOffRed = kStage * kBwdStages;
+  static constexpr int kBars = kOffRed + 2 * kRed;
+  static constexpr int kBytes = kBars + 8 * kBwdStages;
+};
+
+template <typename T, typename TBC>
+__global__ void __launch_bounds__(kThreads, 3) ssm_bwd_kernel(const __grid_constant__ BwdLaunch P) {
+  using S = BwdSmem<T, TBC>;
+  const BwdDir& a = P.dir[blockIdx.z];
+  extern __shared__ __align__(1024) unsigned char smem[];
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::kBars);
+  float* sRed = reinterpret_cast<float*>(smem + S::kOffRed);
+
+  const int b = blockIdx.y;
+  const int c0 = blockIdx.x * kTileCh;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int ch = lane >> 2, nq = lane & 3;
+  const int cl = warp * kChPerWarp + ch;
+  const int c = c0 + cl;
+  const int L = a.L, Dm = a.Dm;
+  if (c0 >= Dm) return;
+  const bool rev = (a.flags & SSM_REVERSE) != 0;
+  const bool comp = rev && (a.flags & SSM_COMPLEMENT);
+  const bool aligned = (a.flags & SSM_ALIGNED_SKIP) != 0;
+  const bool softplus = (a.flags & SSM_DELTA_SOFTPLUS) != 0;
+  const bool has_z = a.has_z != 0, has_D = a.D != nullptr;
+  const bool need_uo = has_D && rev && !aligned;   // skip u at output-frame coordinates
+  const bool need_s = has_D && rev && !aligned;    // dout/z at scan coordinates (skip grad)
+  const int nblk = (L + kChunk - 1) / kChunk;
+  const bool cvalid = c < Dm;
+  const int co = comp ? Dm - 1 - c : c;
+  const int oc0 = comp ? Dm - kTileCh - c0 : c0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kBwdStages; ++s) mbar_init(&bars[s], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  const uint32_t tx_base = 3 * S::kAct + 2 * S::kBC + (has_z ? S::kAct : 0) + (need_uo ? S::kAct : 0) +
+                           (need_s ? (has_z ? 2 : 1) * S::kAct : 0);
+  // it-th issue loads chunk j = nblk-1-it
+  auto issue = [&](int it) {
+    const int j = nblk - 1 - it;
+    unsigned char* st = smem + (it % kBwdStages) * S::kStage;
+    uint64_t* bar = &bars[it % kBwdStages];
+    const int t0 = j * kChunk;
+    const int ot0 = rev ? L - kChunk - t0 : t0;
+    mbar_arrive_expect_tx(bar, tx_base + (j > 0 ? S::kSt : 0));
+    tma_load_3d(st + S::kOffU, &a.tm_u, bar, c0, t0, b);
+    tma_load_3d(st + S::kOffDelta, &a.tm_delta, bar, c0, t0, b);
+    tma_load_3d(st + S::kOffB, &a.tm_B, bar, 0, t0, b);
+    tma_load_3d(st + S::kOffC, &a.tm_C, bar, 0, t0, b);
+    tma_load_3d(st + S::kOffDo, &a.tm_dout, bar, oc0, ot0, b);
+    if (has_z) tma_load_3d(st + S::kOffZo, &a.tm_z, bar, oc0, ot0, b);
+    if (need_uo) tma_load_3d(st + S::kOffUo, &a.tm_u, bar, oc0, ot0, b);
+    if (need_s) {
+      tma_load_3d(st + S::kOffDs, &a.tm_dout, bar, c0, t0, b);
+      if (has_z) tma_load_3d(st + S::kOffZs, &a.tm_z, bar, c0, t0, b);
+    }
+    if (j > 0) tma_load_3d(st + S::kOffS, &a.tm_states, bar, 0, c0, b * nblk + j - 1);
+  };
+  if (threadIdx.x == 0) {
+    const int npre = nblk < kBwdStages ? nblk : kBwdStages;
+    for (int it = 0; it < npre; ++it) issue(it);
+  }
+
+  float An[kNL];
+#pragma unroll
+  for (int k = 0; k < kNL; ++k) An[k] = cvalid ? a.A[(size_t)c * kN + nq * kNL + k] : 0.f;
+  const float bias = (a.bias && cvalid) ? a.bias[c] : 0.f;
+  const float Dsc = (has_D && cvalid) ? a.D[c] : 0.f;                         // skip weight, scan channel
+  const float Dso = (has_D && cvalid) ? a.D[aligned ? c : co] : 0.f;          // skip weight in pre-gate value
+  float fa[kNL] = {0.f, 0.f, 0.f, 0.f};   // f_{t+1} * alpha_{t+1} carried backwards
+  float dA[kNL] = {0.f, 0.f, 0.f, 0.f};
+  float dD_acc = 0.f, db_acc = 0.f;
+  T* du_g = reinterpret_cast<T*>(a.du);
+  T* dd_g = reinterpret_cast<T*>(a.ddelta);
+  T* dz_g = reinterpret_cast<T*>(a.dz);
+  const bool up4 = (lane & 16) != 0, up3 = (lane & 8) != 0, up2 = (lane & 4) != 0;
+
+  for (int it = 0; it < nblk; ++it) {
+    const int j = nblk - 1 - it;
+    const int s = it % kBwdStages;
+    const bool ok = mbar_wait_bounded(&bars[s], (it / kBwdStages) & 1);
+    if (!__syncthreads_and(ok)) {
+      if (threadIdx.x == 0) report(a.status, kStatusTimeout);
+      return;
+    }
+    const unsigned char* st = smem + s * S::kStage;
+    const T* su = reinterpret_cast<const T*>(st + S::kOffU);
+    const T* sd = reinterpret_cast<const T*>(st + S::kOffDelta);
+    const T* szo = reinterpret_cast<const T*>(st + S::kOffZo);
+    const T* sdo = reinterpret_cast<const T*>(st + S::kOffDo);
+    const T* suo = reinterpret_cast<const T*>(st + S::kOffUo);
+    const T* szs = reinterpret_cast<const T*>(st + S::kOffZs);
+    const T* sds = reinterpret_cast<const T*>(st + S::kOffDs);
+    const TBC* sB = reinterpret_cast<const TBC*>(st + S::kOffB);
+    const TBC* sC = reinterpret_cast<const TBC*>(st + S::kOffC);
+    const float* sS = reinterpret_cast<const float*>(st + S::kOffS);
+    float* red = sRed + (it & 1) * (kWarps * kChunk * 32);
+
+    // ---- per-step scalars for the lane's 4 steps
+    float dtv[4], dtx[4], dys[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int tl = nq + 4 * i;
+      const bool valid = j * kChunk + tl < L;
+      const float x = ld_f(su + tl * kTileCh + cl);
+      const float dr = ld_f(sd + tl * kTileCh + cl) + bias;
+      float dt = softplus ? softplus_f(dr) : dr;
+      dt = valid ? dt : 0.f;
+      dtv[i] = dt;
+      dtx[i] = valid ? dt * x : 0.f;
+      const int row = rev ? kChunk - 1 - tl : tl;
+      const int col = comp ? kTileCh - 1 - cl : cl;
+      float g = ld_f(sdo + row * kTileCh + col);
+      if (has_z) g *= act_f(ld_f(szo + row * kTileCh + col), a.gate_act);
+      dys[i] = valid ? g : 0.f;
+    }
+
+    // ---- chunk start state
+    float hs[kNL];
+    if (j > 0) {
+      const float4 h0 = *reinterpret_cast<const float4*>(sS + cl * kN + nq * kNL);
+      hs[0] = h0.x; hs[1] = h0.y; hs[2] = h0.z; hs[3] = h0.w;
+    } else {
+      hs[0] = hs[1] = hs[2] = hs[3] = 0.f;
+    }
+    // Registers hold alpha and alpha*h_{t-1} for half a chunk (8 steps).  The
+    // second half is recomputed from the mid-chunk state and swept first; the
+    // first half is then recomputed from the chunk start and swept.
+    float h[kNL] = {hs[0], hs[1], hs[2], hs[3]};
+    float al[kHalf][kNL], hq[kHalf][kNL];
+    float yv[4] = {0.f, 0.f, 0.f, 0.f};
+    const BwdLane ln{lane, nq, warp, up4, up3, up2, has_z};
+    bwd_forward_half<0, false, true>(ln, h, al, hq, yv, dtv, dtx, dys, An, sB, sC, red);
+    bwd_forward_half<kHalf, true, true>(ln, h, al, hq, yv, dtv, dtx, dys, An, sB, sC, red);
+
+    // ---- dz (needs the recomputed pre-gate output)
+    if (has_z) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int tl = nq + 4 * i;
+        const int t = j * kChunk + tl;
+        if (t < L && cvalid) {
+          const int row = rev ? kChunk - 1 - tl : tl;
+          const int col = comp ? kTileCh - 1 - cl : cl;
+          const int l = rev ? L - 1 - t : t;
+          float pre = yv[i];
+          if (has_D) {
+            const float xs = need_uo ? ld_f(suo + row * kTileCh + col) : ld_f(su + tl * kTileCh + cl);
+            pre = fmaf(Dso, xs, pre);
+          }
+          const float zz = ld_f(szo + row * kTileCh + col);
+          const float g = ld_f(sdo + row * kTileCh + col) * pre * act_grad_f(zz, a.gate_act);
+          st_act(dz_g + ((size_t)b * L + l) * a.z_stride + co, g);
+        }
+      }
+    }
+
+    // ---- reverse sweeps
+    float dxs[4], ddt[4];
+    bwd_reverse_half<kHalf>(ln, al, hq, fa, dA, dtv, dtx, dys, An, sB, sC, su + cl, red, dxs, ddt);
+    h[0] = hs[0]; h[1] = hs[1]; h[2] = hs[2]; h[3] = hs[3];
+    bwd_forward_half<0, true, false>(ln, h, al, hq, yv, dtv, dtx, dys, An, sB, sC, red);
+    bwd_reverse_half<0>(ln, al, hq, fa, dA, dtv, dtx, dys, An, sB, sC, su + cl, red, dxs, ddt);
+
+    // ---- epilogue: du, ddelta, skip grads
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int tl = nq + 4 * i;
+      const int t = j * kChunk + tl;
+      if (t < L && cvalid) {
+        const float x = ld_f(su + tl * kTileCh + cl);
+        float du = dxs[i];
+        if (has_D) {
+          float sg = dys[i];
+          if (need_s) {
+            sg = ld_f(sds + tl * kTileCh + cl);
+            if (has_z) sg *= act_f(ld_f(szs + tl * kTileCh + cl), a.gate_act);
+          }
+          du = fmaf(Dsc, sg, du);
+          dD_acc = fmaf(sg, x, dD_acc);
+        }
+        float g = ddt[i];
+        if (softplus) g *= sigmoid_f(ld_f(sd + tl * kTileCh + cl) + bias);
+        db_acc += g;
+        const size_t off = ((size_t)b * L + t) * Dm + c;
+        st_act(du_g + off, du);
+        st_act(dd_g + off, g);
+      }
+    }
+
+    __syncthreads();  // stage s consumed; red[] complete
+    if (threadIdx.x == 0 && it + kBwdStages < nblk) {
+      fence_proxy_async_smem();
+      issue(it + kBwdStages);
+    }
+    {
+      // sum the 4 warps' partials; thread -> (step, 4 consecutive outputs)
+      const int tl = threadIdx.x >> 3, q4 = threadIdx.x & 7;
+      const int t = j * kChunk + tl;
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int w = 0; w < kWarps; ++w) {
+        const float4 p = *reinterpret_cast<const float4*>(red + (w * kChunk + tl) * 32 + q4 * 4);
+        v.x += p.x; v.y += p.y; v.z += p.z; v.w += p.w;
+      }
+      if (t < L) {
+        float* dst = (q4 < 4 ? a.dB_acc : a.dC_acc) + ((size_t)b * L + t) * a.acc_stride + (q4 & 3) * 4;
+        atomicAdd(reinterpret_cast<float4*>(dst), v);
+      }
+    }
+  }
+
+  // per-(batch row, channel) partials of the parameter gradients
+  dD_acc += __shfl_xor_sync(kFull, dD_acc, 1);
+  dD_acc += __shfl_xor_sync(kFull, dD_acc, 2);
+  db_acc += __shfl_xor_sync(kFull, db_acc, 1);
+  db_acc += __shfl_xor_sync(kFull, db_acc, 2);
+  if (cvalid) {
+    *reinterpret_cast<float4*>(a.dA_part + ((size_t)b * Dm + c) * kN + nq * kNL) =
+        make_float4(dA[0], dA[1], dA[2], dA[3]);
+    if (nq == 0) {
+      a.dD_part[(size_t)b * Dm + c] = dD_acc;
+      a.db_part[(size_t)b * Dm + c] = db_acc;
+    }
+  }
+}
+
+// Sums the per-batch-row partials in batch order (deterministic) and converts
+// the fp32 dB/dC accumulators when B/C are bf16.
+struct FinalizeDir {
+  const float* dA_part;
+  const float* dD_part;
+  const float* db_part;
+  float* dA;
+  float* dD;
+  float* dbias;
+  const float* dB_acc;
+  const float* dC_acc;
+  void* dB;
+  void* dC;
+  int64_t bc_stride;
+  int batch, L, Dm, convert_bc;
+};
+
+}  // namespace ssm
