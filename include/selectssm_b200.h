@@ -169,6 +169,21 @@ SSM_API int ssm_conv1d_act_bwd(const ssm_conv_params_t* p, ssm_stream_t stream);
 
 /* Message for a status code (static storage). */
 SSM_API const char* ssm_strerror(int status);
+/* ---- backward without any device allocation ----
+ * Same result as ssm_bwd, for callers that cannot allocate device memory
+ * (their framework owns the allocator, or allocation is forbidden on their hot
+ * path).  No counterpart in the reference.  The scratch ssm_bwd would take from
+ * p->workspace comes from one static device array of SSM_NOALLOC_SCRATCH_BYTES
+ * per GPU (held until the process exits); p->workspace is ignored and all
+ * inputs and outputs are still the caller's.  Returns SSM_ERR_WORKSPACE when
+ * ssm_workspace_bytes(p) exceeds the array.  The first call on each device
+ * looks up the array's device address; make that call before any stream
+ * capture.  Calls share the array, so calls that overlap on the GPU (other
+ * streams, other host threads, same device) race; the backward re-initialises
+ * every scratch byte it reads, so no state leaks between calls. */
+#define SSM_NOALLOC_SCRATCH_BYTES (8u << 20)
+SSM_API int ssm_bwd_noalloc(const ssm_params_t* p, ssm_stream_t stream);
+
 /* Detail (CUDA error string and call site) of the most recent SSM_ERR_LAUNCH
  * returned on the calling host thread; "" if none. */
 SSM_API const char* ssm_last_error(void);

@@ -34,13 +34,14 @@ SSM_ALIGNED_SKIP = 1 << 3
 ACT_CODES = {None: 0, "none": 0, "silu": 1, "gelu": 2, "relu": 3}
 
 SSM_CHUNK = 16
+NOALLOC_SCRATCH_BYTES = 8 << 20
 DSTATE = 16
 
 # Every symbol include/selectssm_b200.h declares.
 EXPORTED_SYMBOLS = (
     "ssm_workspace_bytes", "ssm_states_elems", "ssm_fwd", "ssm_bwd", "ssm_fwd_bidir", "ssm_bwd_bidir",
     "ssm_conv1d_workspace_bytes", "ssm_conv1d_act_fwd", "ssm_conv1d_act_bwd", "ssm_strerror", "ssm_last_error",
-    "ssm_version",
+    "ssm_version", "ssm_bwd_noalloc",
 )
 
 
@@ -112,6 +113,7 @@ def load(path: str | None = None) -> ctypes.CDLL:
         "ssm_strerror": (ctypes.c_char_p, [ctypes.c_int]),
         "ssm_last_error": (ctypes.c_char_p, []),
         "ssm_version": (ctypes.c_char_p, []),
+        "ssm_bwd_noalloc": (ctypes.c_int, [P, ctypes.c_void_p]),
     }
     for name, (res, args) in sigs.items():
         fn = getattr(lib, name)
