@@ -93,6 +93,12 @@ class ClockSampler:
             self.proc = None
         return self
 
+    def wait_first(self, timeout=3.0):
+        t0 = time.time()
+        while self.proc and not self.rows and time.time() - t0 < timeout:
+            time.sleep(0.02)
+        self.rows.clear()  # keep only samples taken during the timed region
+
     def _read(self):
         for line in self.proc.stdout:
             parts = [p.strip() for p in line.split(",")]
@@ -186,16 +192,19 @@ def run_cpu_sample(seqlen=256, reps=1):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=300)
+    ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--batch", type=int, default=None, help="override batch per GPU (small profiling cases)")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.batch:
+        CFG["batch"] = args.batch
     Bsz, L, D, N = CFG["batch"], CFG["seqlen"], CFG["dim"], CFG["dstate"]
     config = {"workload": "config 2: raw selective-scan op fwd+bwd (softplus dt, D skip, silu gate fused)",
               "batch_per_gpu": Bsz, "global_batch": Bsz * world, "seq_len": L, "d_inner": D, "d_state": N,
@@ -262,6 +271,7 @@ def main():
         dist.barrier()
     torch.cuda.synchronize()
     with ClockSampler(local_rank) as clk:
+        clk.wait_first()
         e0.record(stream)
         for _ in range(args.steps):
             step(t)

@@ -53,18 +53,18 @@ __global__ void finalize_kernel(FinalizeDir f) {
   const int64_t nDN = (int64_t)f.Dm * kN;
   if (i < nDN) {  // dA: sum over batch rows in order
     float s = 0.f;
-    for (int b = 0; b < f.batch; ++b) s += f.dA_part[(int64_t)b * nDN + i];
+    for (int b = 0; b < f.prows; ++b) s += f.dA_part[(int64_t)b * nDN + i];
     f.dA[i] = s;
   }
   if (i < f.Dm) {
     if (f.dD) {
       float s = 0.f;
-      for (int b = 0; b < f.batch; ++b) s += f.dD_part[(int64_t)b * f.Dm + i];
+      for (int b = 0; b < f.prows; ++b) s += f.dD_part[(int64_t)b * f.Dm + i];
       f.dD[i] = s;
     }
     if (f.dbias) {
       float s = 0.f;
-      for (int b = 0; b < f.batch; ++b) s += f.db_part[(int64_t)b * f.Dm + i];
+      for (int b = 0; b < f.prows; ++b) s += f.db_part[(int64_t)b * f.Dm + i];
       f.dbias[i] = s;
     }
   }
@@ -189,10 +189,47 @@ static int check_bwd(const ssm_params_t* p, Geo* g) {
 
 static size_t round256(size_t x) { return (x + 255) & ~size_t(255); }
 
+// Sequence segments.  A (batch row, 32-channel tile) pair is one chain of
+// ceil(L/16) dependent chunks; when there are too few such chains to fill the
+// GPU (measured: about 384 concurrent chains, 2.6 per SM on 148 SMs, saturate
+// it), the sequence is cut into segments that run concurrently, at the cost of
+// one extra recurrence pass for the carries.  The choice depends on the shape
+// only, so results do not depend on the device.
+struct Seg {
+  int nseg, seg_chunks;
+};
+static Seg choose_segments(const Geo& g) {
+  const int nblk = (g.L + kChunk - 1) / kChunk;
+  if (nblk == 0) return {1, 1};
+  const long chains = (long)((g.Dm + kTileCh - 1) / kTileCh) * g.B;
+  const long target = 384;
+  int nseg = chains > 0 ? (int)((target + chains - 1) / chains) : 1;
+  const int max_seg = nblk / 4;  // at least 4 chunks (64 steps) per segment
+  if (nseg > max_seg) nseg = max_seg;
+  if (nseg < 1) nseg = 1;
+  const int seg_chunks = (nblk + nseg - 1) / nseg;
+  return {(nblk + seg_chunks - 1) / seg_chunks, seg_chunks};
+}
+
+static size_t fwd_ws_bytes(const Geo& g) {
+  const Seg sg = choose_segments(g);
+  if (sg.nseg <= 1) return 0;
+  const size_t rows = (size_t)g.B * sg.nseg * g.Dm;
+  return round256(rows * kN * 4) + round256(rows * 4);
+}
+
 static size_t bwd_ws_bytes(const Geo& g) {
-  size_t n = round256((size_t)g.B * g.Dm * kN * 4) + 2 * round256((size_t)g.B * g.Dm * 4);
+  const Seg sg = choose_segments(g);
+  const size_t rows = (size_t)g.B * sg.nseg * g.Dm;
+  size_t n = round256(rows * kN * 4) + 2 * round256(rows * 4);
   if (g.bcbf16) n += 2 * round256((size_t)g.B * g.L * kN * 4);
+  if (sg.nseg > 1) n += round256(rows * kN * 4) + round256(rows * 4);  // segF, segT
   return n;
+}
+
+static size_t ws_bytes(const Geo& g) {
+  const size_t a = fwd_ws_bytes(g), b = bwd_ws_bytes(g);
+  return a > b ? a : b;
 }
 
 // ---------------------------------------------------------------- forward launch
@@ -221,22 +258,42 @@ static int fill_fwd_dir(const ssm_params_t* p, const Geo& g, FwdDir* d) {
   d->flags = p->flags;
   d->gate_act = p->z ? p->gate_act : SSM_ACT_NONE;
   d->has_z = p->z != nullptr;
+  const Seg sg = choose_segments(g);
+  d->nseg = sg.nseg;
+  d->seg_chunks = sg.seg_chunks;
+  if (sg.nseg > 1) {
+    char* ws = static_cast<char*>(p->workspace);
+    d->segH = reinterpret_cast<float*>(ws);
+    d->segT = reinterpret_cast<float*>(ws + round256((size_t)g.B * sg.nseg * g.Dm * kN * 4));
+  }
   return SSM_OK;
 }
 
 template <typename T, typename TBC>
-static int launch_fwd_t(const FwdLaunch& L, int ndir, const Geo& g, cudaStream_t s) {
+static int launch_fwd_t(FwdLaunch& L, int ndir, const Geo& g, cudaStream_t s) {
   using S = FwdSmem<T, TBC>;
-  auto kern = ssm_fwd_kernel<T, TBC>;
+  const int nseg = L.dir[0].nseg;
+  dim3 grid((g.Dm + kTileCh - 1) / kTileCh, g.B, 1);
+  if (nseg > 1) {  // segment pre-pass: end state of every segment but the last
+    auto agg = ssm_fwd_kernel<T, TBC, true>;
+    SSM_CUDA_CHECK(cudaFuncSetAttribute(agg, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kBytes),
+                   "cudaFuncSetAttribute(ssm_fwd_kernel<agg>)");
+    L.zdiv = nseg - 1;
+    grid.z = ndir * (nseg - 1);
+    agg<<<grid, kThreads, S::kBytes, s>>>(L);
+    SSM_CUDA_CHECK(cudaGetLastError(), "launch ssm_fwd_kernel<agg>");
+  }
+  auto kern = ssm_fwd_kernel<T, TBC, false>;
   SSM_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kBytes),
                  "cudaFuncSetAttribute(ssm_fwd_kernel)");
-  dim3 grid((g.Dm + kTileCh - 1) / kTileCh, g.B, ndir);
+  L.zdiv = nseg;
+  grid.z = ndir * nseg;
   kern<<<grid, kThreads, S::kBytes, s>>>(L);
   SSM_CUDA_CHECK(cudaGetLastError(), "launch ssm_fwd_kernel");
   return SSM_OK;
 }
 
-static int launch_fwd(const FwdLaunch& L, int ndir, const Geo& g, cudaStream_t s) {
+static int launch_fwd(FwdLaunch& L, int ndir, const Geo& g, cudaStream_t s) {
   if (!g.bf16 && !g.bcbf16) return launch_fwd_t<float, float>(L, ndir, g, s);
   if (!g.bf16 && g.bcbf16) return launch_fwd_t<float, __nv_bfloat16>(L, ndir, g, s);
   if (g.bf16 && !g.bcbf16) return launch_fwd_t<__nv_bfloat16, float>(L, ndir, g, s);
@@ -245,17 +302,26 @@ static int launch_fwd(const FwdLaunch& L, int ndir, const Geo& g, cudaStream_t s
 
 // ---------------------------------------------------------------- backward launch
 struct BwdWs {
-  float *dA_part, *dD_part, *db_part, *dB_acc, *dC_acc;
+  float *dA_part, *dD_part, *db_part, *dB_acc, *dC_acc, *segF, *segT;
   int64_t acc_stride;
 };
 
 static void carve_ws(const ssm_params_t* p, const Geo& g, char* ws, BwdWs* w) {
+  const Seg sg = choose_segments(g);
+  const size_t rows = (size_t)g.B * sg.nseg * g.Dm;
   w->dA_part = reinterpret_cast<float*>(ws);
-  ws += round256((size_t)g.B * g.Dm * kN * 4);
+  ws += round256(rows * kN * 4);
   w->dD_part = reinterpret_cast<float*>(ws);
-  ws += round256((size_t)g.B * g.Dm * 4);
+  ws += round256(rows * 4);
   w->db_part = reinterpret_cast<float*>(ws);
-  ws += round256((size_t)g.B * g.Dm * 4);
+  ws += round256(rows * 4);
+  w->segF = w->segT = nullptr;
+  if (sg.nseg > 1) {
+    w->segF = reinterpret_cast<float*>(ws);
+    ws += round256(rows * kN * 4);
+    w->segT = reinterpret_cast<float*>(ws);
+    ws += round256(rows * 4);
+  }
   if (g.bcbf16) {
     w->dB_acc = reinterpret_cast<float*>(ws);
     ws += round256((size_t)g.B * g.L * kN * 4);
@@ -304,22 +370,43 @@ static int fill_bwd_dir(const ssm_params_t* p, const Geo& g, const BwdWs& w, Bwd
   d->flags = p->flags;
   d->gate_act = p->z ? p->gate_act : SSM_ACT_NONE;
   d->has_z = p->z != nullptr;
+  const Seg sg = choose_segments(g);
+  d->nseg = sg.nseg;
+  d->seg_chunks = sg.seg_chunks;
+  d->segF = w.segF;
+  d->segT = w.segT;
   return SSM_OK;
 }
 
 template <typename T, typename TBC>
-static int launch_bwd_t(const BwdLaunch& L, int ndir, const Geo& g, cudaStream_t s) {
+static int launch_bwd_t(BwdLaunch& L, int ndir, const Geo& g, cudaStream_t s) {
   using S = BwdSmem<T, TBC>;
+  const int nseg = L.dir[0].nseg;
+  dim3 grid((g.Dm + kTileCh - 1) / kTileCh, g.B, 1);
+  if (nseg > 1) {  // segment pre-pass: adjoint carried out of every segment but the first
+    using SA = BwdAggSmem<T, TBC>;
+    auto agg = ssm_bwd_agg_kernel<T, TBC>;
+    SSM_CUDA_CHECK(cudaFuncSetAttribute(agg, cudaFuncAttributeMaxDynamicSharedMemorySize, SA::kBytes),
+                   "cudaFuncSetAttribute(ssm_bwd_agg_kernel)");
+    L.zdiv = nseg - 1;
+    grid.z = ndir * (nseg - 1);
+    agg<<<grid, kThreads, SA::kBytes, s>>>(L);
+    SSM_CUDA_CHECK(cudaGetLastError(), "launch ssm_bwd_agg_kernel");
+    dim3 fgrid((g.Dm * kN + 255) / 256, ndir, g.B);
+    ssm_bwd_fold_kernel<<<fgrid, 256, 0, s>>>(L);
+    SSM_CUDA_CHECK(cudaGetLastError(), "launch ssm_bwd_fold_kernel");
+  }
   auto kern = ssm_bwd_kernel<T, TBC>;
   SSM_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kBytes),
                  "cudaFuncSetAttribute(ssm_bwd_kernel)");
-  dim3 grid((g.Dm + kTileCh - 1) / kTileCh, g.B, ndir);
+  L.zdiv = nseg;
+  grid.z = ndir * nseg;
   kern<<<grid, kThreads, S::kBytes, s>>>(L);
   SSM_CUDA_CHECK(cudaGetLastError(), "launch ssm_bwd_kernel");
   return SSM_OK;
 }
 
-static int launch_bwd(const BwdLaunch& L, int ndir, const Geo& g, cudaStream_t s) {
+static int launch_bwd(BwdLaunch& L, int ndir, const Geo& g, cudaStream_t s) {
   if (!g.bf16 && !g.bcbf16) return launch_bwd_t<float, float>(L, ndir, g, s);
   if (!g.bf16 && g.bcbf16) return launch_bwd_t<float, __nv_bfloat16>(L, ndir, g, s);
   if (g.bf16 && !g.bcbf16) return launch_bwd_t<__nv_bfloat16, float>(L, ndir, g, s);
@@ -351,6 +438,7 @@ static int launch_finalize(const ssm_params_t* p, const Geo& g, const BwdWs& w, 
   f.dB = p->dB;
   f.dC = p->dC;
   f.bc_stride = g.bs;
+  f.prows = g.B * choose_segments(g).nseg;
   f.batch = g.B;
   f.L = g.L;
   f.Dm = g.Dm;
@@ -386,7 +474,7 @@ size_t ssm_states_elems(const ssm_params_t* p) {
 size_t ssm_workspace_bytes(const ssm_params_t* p) {
   Geo g;
   if (check_common(p, &g) != SSM_OK) return 0;
-  return bwd_ws_bytes(g);
+  return ws_bytes(g);
 }
 
 int ssm_fwd(const ssm_params_t* p, ssm_stream_t stream) { return ssm_fwd_bidir(p, nullptr, stream); }
@@ -403,6 +491,12 @@ int ssm_fwd_bidir(const ssm_params_t* fwd, const ssm_params_t* rev, ssm_stream_t
   if ((int64_t)g.B * g.L * g.Dm == 0) return SSM_OK;
   st = bind_device(fwd->u);
   if (st) return st;
+  const size_t need = fwd_ws_bytes(g);
+  for (const ssm_params_t* q : {fwd, rev}) {
+    if (!q) continue;
+    if (need && (!q->workspace || q->workspace_bytes < need)) return SSM_ERR_WORKSPACE;
+    if (reinterpret_cast<uintptr_t>(q->workspace) & 255u) return SSM_ERR_ALIGN;
+  }
   FwdLaunch args;
   std::memset(&args, 0, sizeof(args));
   st = fill_fwd_dir(fwd, g, &args.dir[0]);

@@ -47,11 +47,15 @@ struct FwdDir {
   void* out;
   float* states;
   int32_t* status;
+  float* segH;    // (B, nseg, D, 16) segment end states from a zero start
+  float* segT;    // (B, nseg, D) sum of dt over each segment
   int64_t out_stride;
   int L, Dm, flags, gate_act, has_z;
+  int nseg, seg_chunks;  // sequence segments (each seg_chunks chunks of 16 steps)
 };
 struct FwdLaunch {
   FwdDir dir[2];
+  int zdiv;  // blockIdx.z = direction * zdiv + segment
 };
 
 struct BwdDir {
@@ -64,15 +68,19 @@ struct BwdDir {
   void* dz;
   float* dB_acc;   // fp32 accumulation target for dB (row stride acc_stride)
   float* dC_acc;
-  float* dA_part;  // (B, D, 16)
-  float* dD_part;  // (B, D)
-  float* db_part;  // (B, D)
+  float* dA_part;  // (B, nseg, D, 16)
+  float* dD_part;  // (B, nseg, D)
+  float* db_part;  // (B, nseg, D)
+  float* segF;     // (B, nseg, D, 16) adjoint carried out of each segment's first step, zero start
+  float* segT;     // (B, nseg, D) sum of dt over each segment
   int32_t* status;
   int64_t z_stride, acc_stride;
   int L, Dm, flags, gate_act, has_z;
+  int nseg, seg_chunks;
 };
 struct BwdLaunch {
   BwdDir dir[2];
+  int zdiv;
 };
 
 template <typename T>
@@ -92,10 +100,15 @@ struct FwdSmem {
   static constexpr int kBytes = kBars + 8 * kFwdStages;
 };
 
-template <typename T, typename TBC>
+// AGG: the segment pre-pass.  It runs the recurrence over one segment from a
+// zero state and writes only the segment's end state and sum of dt (no C, z,
+// output or checkpoints); the main pass then starts segment s from the states
+// of segments 0..s-1 folded together (h <- exp(A sum dt) h + H).
+template <typename T, typename TBC, bool AGG>
 __global__ void __launch_bounds__(kThreads, 3) ssm_fwd_kernel(const __grid_constant__ FwdLaunch P) {
   using S = FwdSmem<T, TBC>;
-  const FwdDir& a = P.dir[blockIdx.z];
+  const FwdDir& a = P.dir[blockIdx.z / P.zdiv];
+  const int seg = blockIdx.z % P.zdiv;
   extern __shared__ __align__(1024) unsigned char smem[];
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::kBars);
 
@@ -114,6 +127,9 @@ __global__ void __launch_bounds__(kThreads, 3) ssm_fwd_kernel(const __grid_const
   const bool has_z = a.has_z != 0, has_D = a.D != nullptr;
   const bool need_uo = has_D && rev && !aligned;
   const int nblk = (L + kChunk - 1) / kChunk;
+  const int j0 = seg * a.seg_chunks;
+  const int j1 = min(nblk, j0 + a.seg_chunks);
+  const int nloc = j1 - j0;
   const bool cvalid = c < Dm;
   const int co = comp ? Dm - 1 - c : c;                 // output-frame channel
   const int oc0 = comp ? Dm - kTileCh - c0 : c0;        // output-frame tile start
@@ -124,23 +140,26 @@ __global__ void __launch_bounds__(kThreads, 3) ssm_fwd_kernel(const __grid_const
   }
   __syncthreads();
 
-  const uint32_t tx = 2 * S::kAct + 2 * S::kBC + (has_z ? S::kAct : 0) + (need_uo ? S::kAct : 0);
-  auto issue = [&](int j) {
-    unsigned char* st = smem + (j % kFwdStages) * S::kStage;
-    uint64_t* bar = &bars[j % kFwdStages];
-    const int t0 = j * kChunk;
+  const uint32_t tx = AGG ? 2 * S::kAct + S::kBC
+                          : 2 * S::kAct + 2 * S::kBC + (has_z ? S::kAct : 0) + (need_uo ? S::kAct : 0);
+  auto issue = [&](int jl) {  // local chunk index within the segment
+    unsigned char* st = smem + (jl % kFwdStages) * S::kStage;
+    uint64_t* bar = &bars[jl % kFwdStages];
+    const int t0 = (j0 + jl) * kChunk;
     const int ot0 = rev ? L - kChunk - t0 : t0;
     mbar_arrive_expect_tx(bar, tx);
     tma_load_3d(st + S::kOffU, &a.tm_u, bar, c0, t0, b);
     tma_load_3d(st + S::kOffDelta, &a.tm_delta, bar, c0, t0, b);
     tma_load_3d(st + S::kOffB, &a.tm_B, bar, 0, t0, b);
-    tma_load_3d(st + S::kOffC, &a.tm_C, bar, 0, t0, b);
-    if (has_z) tma_load_3d(st + S::kOffZ, &a.tm_z, bar, oc0, ot0, b);
-    if (need_uo) tma_load_3d(st + S::kOffUo, &a.tm_u, bar, oc0, ot0, b);
+    if (!AGG) {
+      tma_load_3d(st + S::kOffC, &a.tm_C, bar, 0, t0, b);
+      if (has_z) tma_load_3d(st + S::kOffZ, &a.tm_z, bar, oc0, ot0, b);
+      if (need_uo) tma_load_3d(st + S::kOffUo, &a.tm_u, bar, oc0, ot0, b);
+    }
   };
   if (threadIdx.x == 0) {
-    const int npre = nblk < kFwdStages ? nblk : kFwdStages;
-    for (int j = 0; j < npre; ++j) issue(j);
+    const int npre = nloc < kFwdStages ? nloc : kFwdStages;
+    for (int jl = 0; jl < npre; ++jl) issue(jl);
   }
 
   // per-lane constants
@@ -150,11 +169,24 @@ __global__ void __launch_bounds__(kThreads, 3) ssm_fwd_kernel(const __grid_const
   const float bias = (a.bias && cvalid) ? a.bias[c] : 0.f;
   const float Dsk = (has_D && cvalid) ? a.D[aligned ? c : co] : 0.f;
   float h[kNL] = {0.f, 0.f, 0.f, 0.f};
+  if (!AGG && cvalid) {  // fold the states of the preceding segments
+    for (int sp = 0; sp < seg; ++sp) {
+      const size_t r = (size_t)b * a.nseg + sp;
+      const float T = a.segT[r * Dm + c];
+      const float4 H = *reinterpret_cast<const float4*>(a.segH + (r * Dm + c) * kN + nq * kNL);
+      h[0] = fmaf(ex2(A2[0] * T), h[0], H.x);
+      h[1] = fmaf(ex2(A2[1] * T), h[1], H.y);
+      h[2] = fmaf(ex2(A2[2] * T), h[2], H.z);
+      h[3] = fmaf(ex2(A2[3] * T), h[3], H.w);
+    }
+  }
+  float tsum = 0.f;  // AGG: sum of this lane's dt
   T* out = reinterpret_cast<T*>(a.out);
 
-  for (int j = 0; j < nblk; ++j) {
-    const int s = j % kFwdStages;
-    const bool ok = mbar_wait_bounded(&bars[s], (j / kFwdStages) & 1);
+  for (int j = j0; j < j1; ++j) {
+    const int jl = j - j0;
+    const int s = jl % kFwdStages;
+    const bool ok = mbar_wait_bounded(&bars[s], (jl / kFwdStages) & 1);
     if (!__syncthreads_and(ok)) {
       if (threadIdx.x == 0) report(a.status, kStatusTimeout);
       return;
@@ -179,6 +211,26 @@ __global__ void __launch_bounds__(kThreads, 3) ssm_fwd_kernel(const __grid_const
       dt = valid ? dt : 0.f;
       dtv[i] = dt;
       dtx[i] = valid ? dt * x : 0.f;
+      tsum += dt;
+    }
+    if (AGG) {
+#pragma unroll
+      for (int tl = 0; tl < kChunk; ++tl) {
+        const int src = (lane & ~3) | (tl & 3);
+        const float dt = __shfl_sync(kFull, dtv[tl >> 2], src);
+        const float dx = __shfl_sync(kFull, dtx[tl >> 2], src);
+        const float4 Bv = ld4(sB + tl * kN + nq * kNL);
+        h[0] = fmaf(ex2(A2[0] * dt), h[0], Bv.x * dx);
+        h[1] = fmaf(ex2(A2[1] * dt), h[1], Bv.y * dx);
+        h[2] = fmaf(ex2(A2[2] * dt), h[2], Bv.z * dx);
+        h[3] = fmaf(ex2(A2[3] * dt), h[3], Bv.w * dx);
+      }
+      __syncthreads();
+      if (threadIdx.x == 0 && jl + kFwdStages < nloc) {
+        fence_proxy_async_smem();
+        issue(jl + kFwdStages);
+      }
+      continue;
     }
 
     float yv[4] = {0.f, 0.f, 0.f, 0.f};
@@ -223,9 +275,18 @@ __global__ void __launch_bounds__(kThreads, 3) ssm_fwd_kernel(const __grid_const
       }
     }
     __syncthreads();  // every warp is done with stage s
-    if (threadIdx.x == 0 && j + kFwdStages < nblk) {
+    if (threadIdx.x == 0 && jl + kFwdStages < nloc) {
       fence_proxy_async_smem();
-      issue(j + kFwdStages);
+      issue(jl + kFwdStages);
+    }
+  }
+  if (AGG) {
+    tsum += __shfl_xor_sync(kFull, tsum, 1);
+    tsum += __shfl_xor_sync(kFull, tsum, 2);
+    if (cvalid) {
+      const size_t r = (size_t)b * a.nseg + seg;
+      *reinterpret_cast<float4*>(a.segH + (r * Dm + c) * kN + nq * kNL) = make_float4(h[0], h[1], h[2], h[3]);
+      if (nq == 0) a.segT[r * Dm + c] = tsum;
     }
   }
 }
@@ -355,7 +416,8 @@ struct BwdSmem {
 template <typename T, typename TBC>
 __global__ void __launch_bounds__(kThreads, 3) ssm_bwd_kernel(const __grid_constant__ BwdLaunch P) {
   using S = BwdSmem<T, TBC>;
-  const BwdDir& a = P.dir[blockIdx.z];
+  const BwdDir& a = P.dir[blockIdx.z / P.zdiv];
+  const int seg = blockIdx.z % P.zdiv;
   extern __shared__ __align__(1024) unsigned char smem[];
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::kBars);
   float* sRed = reinterpret_cast<float*>(smem + S::kOffRed);
@@ -376,6 +438,8 @@ __global__ void __launch_bounds__(kThreads, 3) ssm_bwd_kernel(const __grid_const
   const bool need_uo = has_D && rev && !aligned;   // skip u at output-frame coordinates
   const bool need_s = has_D && rev && !aligned;    // dout/z at scan coordinates (skip grad)
   const int nblk = (L + kChunk - 1) / kChunk;
+  const int j1 = min(nblk, (seg + 1) * a.seg_chunks);
+  const int nloc = j1 - seg * a.seg_chunks;
   const bool cvalid = c < Dm;
   const int co = comp ? Dm - 1 - c : c;
   const int oc0 = comp ? Dm - kTileCh - c0 : c0;
@@ -388,9 +452,9 @@ __global__ void __launch_bounds__(kThreads, 3) ssm_bwd_kernel(const __grid_const
 
   const uint32_t tx_base = 3 * S::kAct + 2 * S::kBC + (has_z ? S::kAct : 0) + (need_uo ? S::kAct : 0) +
                            (need_s ? (has_z ? 2 : 1) * S::kAct : 0);
-  // it-th issue loads chunk j = nblk-1-it
+  // it-th issue loads chunk j = j1-1-it (the segment's chunks, last first)
   auto issue = [&](int it) {
-    const int j = nblk - 1 - it;
+    const int j = j1 - 1 - it;
     unsigned char* st = smem + (it % kBwdStages) * S::kStage;
     uint64_t* bar = &bars[it % kBwdStages];
     const int t0 = j * kChunk;
@@ -410,7 +474,7 @@ __global__ void __launch_bounds__(kThreads, 3) ssm_bwd_kernel(const __grid_const
     if (j > 0) tma_load_3d(st + S::kOffS, &a.tm_states, bar, 0, c0, b * nblk + j - 1);
   };
   if (threadIdx.x == 0) {
-    const int npre = nblk < kBwdStages ? nblk : kBwdStages;
+    const int npre = nloc < kBwdStages ? nloc : kBwdStages;
     for (int it = 0; it < npre; ++it) issue(it);
   }
 
@@ -421,6 +485,10 @@ __global__ void __launch_bounds__(kThreads, 3) ssm_bwd_kernel(const __grid_const
   const float Dsc = (has_D && cvalid) ? a.D[c] : 0.f;                         // skip weight, scan channel
   const float Dso = (has_D && cvalid) ? a.D[aligned ? c : co] : 0.f;          // skip weight in pre-gate value
   float fa[kNL] = {0.f, 0.f, 0.f, 0.f};   // f_{t+1} * alpha_{t+1} carried backwards
+  if (a.nseg > 1 && cvalid) {  // adjoint entering this segment from the later ones
+    const float4 F = *reinterpret_cast<const float4*>(a.segF + (((size_t)b * a.nseg + seg) * Dm + c) * kN + nq * kNL);
+    fa[0] = F.x; fa[1] = F.y; fa[2] = F.z; fa[3] = F.w;
+  }
   float dA[kNL] = {0.f, 0.f, 0.f, 0.f};
   float dD_acc = 0.f, db_acc = 0.f;
   T* du_g = reinterpret_cast<T*>(a.du);
@@ -428,8 +496,8 @@ __global__ void __launch_bounds__(kThreads, 3) ssm_bwd_kernel(const __grid_const
   T* dz_g = reinterpret_cast<T*>(a.dz);
   const bool up4 = (lane & 16) != 0, up3 = (lane & 8) != 0, up2 = (lane & 4) != 0;
 
-  for (int it = 0; it < nblk; ++it) {
-    const int j = nblk - 1 - it;
+  for (int it = 0; it < nloc; ++it) {
+    const int j = j1 - 1 - it;
     const int s = it % kBwdStages;
     const bool ok = mbar_wait_bounded(&bars[s], (it / kBwdStages) & 1);
     if (!__syncthreads_and(ok)) {
@@ -542,7 +610,7 @@ __global__ void __launch_bounds__(kThreads, 3) ssm_bwd_kernel(const __grid_const
     }
 
     __syncthreads();  // stage s consumed; red[] complete
-    if (threadIdx.x == 0 && it + kBwdStages < nblk) {
+    if (threadIdx.x == 0 && it + kBwdStages < nloc) {
       fence_proxy_async_smem();
       issue(it + kBwdStages);
     }
@@ -569,12 +637,157 @@ __global__ void __launch_bounds__(kThreads, 3) ssm_bwd_kernel(const __grid_const
   db_acc += __shfl_xor_sync(kFull, db_acc, 1);
   db_acc += __shfl_xor_sync(kFull, db_acc, 2);
   if (cvalid) {
-    *reinterpret_cast<float4*>(a.dA_part + ((size_t)b * Dm + c) * kN + nq * kNL) =
-        make_float4(dA[0], dA[1], dA[2], dA[3]);
+    const size_t r = (size_t)b * a.nseg + blockIdx.z % P.zdiv;
+    *reinterpret_cast<float4*>(a.dA_part + (r * Dm + c) * kN + nq * kNL) = make_float4(dA[0], dA[1], dA[2], dA[3]);
     if (nq == 0) {
-      a.dD_part[(size_t)b * Dm + c] = dD_acc;
-      a.db_part[(size_t)b * Dm + c] = db_acc;
+      a.dD_part[r * Dm + c] = dD_acc;
+      a.db_part[r * Dm + c] = db_acc;
     }
+  }
+}
+
+// Backward segment pre-pass: for segment s >= 1 runs the adjoint recurrence
+// f_t = C_t dy_t + f_{t+1} alpha_{t+1} over the segment from a zero carry and
+// writes the carry leaving its first step (f alpha) and the segment's sum of
+// dt.  Only delta, C, dout (and z for the gate) are read.
+template <typename T, typename TBC>
+struct BwdAggSmem {
+  static constexpr int kAct = kChunk * kTileCh * (int)sizeof(T);
+  static constexpr int kBC = kChunk * kN * (int)sizeof(TBC);
+  static constexpr int kOffDelta = 0, kOffDo = kAct, kOffZo = 2 * kAct, kOffC = 3 * kAct;
+  static constexpr int kStage = 3 * kAct + kBC;
+  static constexpr int kBars = kStage * kFwdStages;
+  static constexpr int kBytes = kBars + 8 * kFwdStages;
+};
+
+template <typename T, typename TBC>
+__global__ void __launch_bounds__(kThreads, 4) ssm_bwd_agg_kernel(const __grid_constant__ BwdLaunch P) {
+  using S = BwdAggSmem<T, TBC>;
+  const BwdDir& a = P.dir[blockIdx.z / P.zdiv];
+  const int seg = 1 + blockIdx.z % P.zdiv;  // segments 1 .. nseg-1
+  extern __shared__ __align__(1024) unsigned char smem[];
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::kBars);
+
+  const int b = blockIdx.y;
+  const int c0 = blockIdx.x * kTileCh;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int ch = lane >> 2, nq = lane & 3;
+  const int cl = warp * kChPerWarp + ch;
+  const int c = c0 + cl;
+  const int L = a.L, Dm = a.Dm;
+  if (c0 >= Dm) return;
+  const bool rev = (a.flags & SSM_REVERSE) != 0;
+  const bool comp = rev && (a.flags & SSM_COMPLEMENT);
+  const bool softplus = (a.flags & SSM_DELTA_SOFTPLUS) != 0;
+  const bool has_z = a.has_z != 0;
+  const int nblk = (L + kChunk - 1) / kChunk;
+  const int j0 = seg * a.seg_chunks;
+  const int j1 = min(nblk, j0 + a.seg_chunks);
+  const int nloc = j1 - j0;
+  const bool cvalid = c < Dm;
+  const int oc0 = comp ? Dm - kTileCh - c0 : c0;
+  const int col = comp ? kTileCh - 1 - cl : cl;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kFwdStages; ++s) mbar_init(&bars[s], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  const uint32_t tx = 2 * S::kAct + S::kBC + (has_z ? S::kAct : 0);
+  auto issue = [&](int it) {
+    const int j = j1 - 1 - it;
+    unsigned char* st = smem + (it % kFwdStages) * S::kStage;
+    uint64_t* bar = &bars[it % kFwdStages];
+    const int t0 = j * kChunk;
+    const int ot0 = rev ? L - kChunk - t0 : t0;
+    mbar_arrive_expect_tx(bar, tx);
+    tma_load_3d(st + S::kOffDelta, &a.tm_delta, bar, c0, t0, b);
+    tma_load_3d(st + S::kOffC, &a.tm_C, bar, 0, t0, b);
+    tma_load_3d(st + S::kOffDo, &a.tm_dout, bar, oc0, ot0, b);
+    if (has_z) tma_load_3d(st + S::kOffZo, &a.tm_z, bar, oc0, ot0, b);
+  };
+  if (threadIdx.x == 0) {
+    const int npre = nloc < kFwdStages ? nloc : kFwdStages;
+    for (int it = 0; it < npre; ++it) issue(it);
+  }
+  float A2[kNL];
+#pragma unroll
+  for (int k = 0; k < kNL; ++k) A2[k] = cvalid ? a.A[(size_t)c * kN + nq * kNL + k] * kLog2e : 0.f;
+  const float bias = (a.bias && cvalid) ? a.bias[c] : 0.f;
+  float fa[kNL] = {0.f, 0.f, 0.f, 0.f};
+  float tsum = 0.f;
+  for (int it = 0; it < nloc; ++it) {
+    const int j = j1 - 1 - it;
+    const int s = it % kFwdStages;
+    const bool ok = mbar_wait_bounded(&bars[s], (it / kFwdStages) & 1);
+    if (!__syncthreads_and(ok)) {
+      if (threadIdx.x == 0) report(a.status, kStatusTimeout);
+      return;
+    }
+    const unsigned char* st = smem + s * S::kStage;
+    const T* sd = reinterpret_cast<const T*>(st + S::kOffDelta);
+    const T* sdo = reinterpret_cast<const T*>(st + S::kOffDo);
+    const T* szo = reinterpret_cast<const T*>(st + S::kOffZo);
+    const TBC* sC = reinterpret_cast<const TBC*>(st + S::kOffC);
+    float dtv[4], dys[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int tl = nq + 4 * i;
+      const bool valid = j * kChunk + tl < L;
+      const float dr = ld_f(sd + tl * kTileCh + cl) + bias;
+      const float dt = softplus ? softplus_f(dr) : dr;
+      dtv[i] = valid ? dt : 0.f;
+      tsum += dtv[i];
+      const int row = rev ? kChunk - 1 - tl : tl;
+      float g = ld_f(sdo + row * kTileCh + col);
+      if (has_z) g *= act_f(ld_f(szo + row * kTileCh + col), a.gate_act);
+      dys[i] = valid ? g : 0.f;
+    }
+#pragma unroll
+    for (int tl = kChunk - 1; tl >= 0; --tl) {
+      const int src = (lane & ~3) | (tl & 3);
+      const float dt = __shfl_sync(kFull, dtv[tl >> 2], src);
+      const float dy = __shfl_sync(kFull, dys[tl >> 2], src);
+      const float4 Cv = ld4(sC + tl * kN + nq * kNL);
+      fa[0] = fmaf(Cv.x, dy, fa[0]) * ex2(A2[0] * dt);
+      fa[1] = fmaf(Cv.y, dy, fa[1]) * ex2(A2[1] * dt);
+      fa[2] = fmaf(Cv.z, dy, fa[2]) * ex2(A2[2] * dt);
+      fa[3] = fmaf(Cv.w, dy, fa[3]) * ex2(A2[3] * dt);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0 && it + kFwdStages < nloc) {
+      fence_proxy_async_smem();
+      issue(it + kFwdStages);
+    }
+  }
+  tsum += __shfl_xor_sync(kFull, tsum, 1);
+  tsum += __shfl_xor_sync(kFull, tsum, 2);
+  if (cvalid) {
+    const size_t r = (size_t)b * a.nseg + seg;
+    *reinterpret_cast<float4*>(a.segF + (r * Dm + c) * kN + nq * kNL) = make_float4(fa[0], fa[1], fa[2], fa[3]);
+    if (nq == 0) a.segT[r * Dm + c] = tsum;
+  }
+}
+
+// Turns the per-segment adjoint aggregates into the adjoint entering each
+// segment from the right, in place: carry_{S-1} = 0,
+// carry_s = exp(A T_{s+1}) carry_{s+1} + F_{s+1}.  One thread per (b, d, n).
+// Grid: (channel*state blocks, direction, batch row).
+__global__ void ssm_bwd_fold_kernel(const __grid_constant__ BwdLaunch P) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const BwdDir& a = P.dir[blockIdx.y];
+  if (i >= (int64_t)a.Dm * kN) return;
+  const int b = blockIdx.z;
+  const int c = (int)(i / kN), n = (int)(i % kN);
+  const float A2 = a.A[(size_t)c * kN + n] * kLog2e;
+  float carry = 0.f;
+  for (int sg = a.nseg - 1; sg >= 0; --sg) {
+    const size_t r = (size_t)b * a.nseg + sg;
+    float* Fp = a.segF + (r * a.Dm + c) * kN + n;
+    const float F = sg > 0 ? *Fp : 0.f;
+    const float T = sg > 0 ? a.segT[r * a.Dm + c] : 0.f;
+    *Fp = carry;
+    carry = fmaf(ex2(A2 * T), carry, F);
   }
 }
 
@@ -592,6 +805,7 @@ struct FinalizeDir {
   void* dB;
   void* dC;
   int64_t bc_stride;
+  int prows;  // rows of partials (batch x segments)
   int batch, L, Dm, convert_bc;
 };
 

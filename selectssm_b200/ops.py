@@ -218,7 +218,9 @@ class _SelectiveScanFn(torch.autograd.Function):
         out = torch.empty(pr.shape, dtype=pr.dtype, device=pr.u.device)
         states = pr.new_states()
         p = pr.params(out=out, out_stride=pr.shape[2], states=states)
+        ws = _workspace(p, pr.u.device)  # segment carries (long sequences, few channels)
         _lib.check(_lib.load().ssm_fwd(ctypes_byref(p), _stream()), "ssm_fwd")
+        del ws
         ctx.pr = pr
         ctx.delta_broadcast = delta.shape[-1] == 1 and u.shape[-1] != 1
         ctx.save_for_backward(states)
@@ -318,7 +320,9 @@ class _BidirScanFn(torch.autograd.Function):
         sf, sr = prf.new_states(), prr.new_states()
         pf = prf.params(out=out[..., :Dm], out_stride=2 * Dm, states=sf)
         pr = prr.params(out=out[..., Dm:], out_stride=2 * Dm, states=sr)
+        wsf, wsr = _workspace(pf, prf.u.device), _workspace(pr, prr.u.device)
         _lib.check(_lib.load().ssm_fwd_bidir(ctypes_byref(pf), ctypes_byref(pr), _stream()), "ssm_fwd_bidir")
+        del wsf, wsr
         ctx.prs = (prf, prr)
         ctx.save_for_backward(sf, sr)
         return out

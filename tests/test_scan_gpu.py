@@ -194,3 +194,23 @@ def test_long_sequence_states_roundtrip(cuda):
     y = S.ssm_chunked_scan(to_t(inp["u"], cuda), to_t(inp["A"], cuda), to_t(inp["B"], cuda), to_t(inp["C"], cuda),
                            to_t(dt, cuda))
     assert relerr(to_np(y), ref) < 1e-4
+
+
+@pytest.mark.parametrize("rev,comp", [(False, False), (True, True)])
+def test_segmented_long_sequence_fwd_bwd(cuda, rev, comp):
+    """Few channels and a long sequence: the kernels cut the sequence into
+    concurrent segments joined by carried states / adjoints."""
+    import selectssm_b200 as S
+    Bsz, L, D = 1, 1100, 64
+    inp = make(Bsz, L, D, 21, torch.float32)
+    kw = dict(D=inp["D"], z=inp["z"], delta_bias=inp["bias"], delta_softplus=True, reverse=rev, complement=comp)
+    ref_out = O.selective_scan_fwd(inp["u"], inp["delta"], inp["A"], inp["B"], inp["C"], **kw)
+    ref = O.selective_scan_bwd(inp["u"], inp["delta"], inp["A"], inp["B"], inp["C"], inp["dout"], **kw)
+    t = {k: to_t(inp[k], cuda).requires_grad_() for k in ("u", "delta", "A", "B", "C", "D", "bias", "z")}
+    out = S.selective_scan(t["u"], t["delta"], t["A"], t["B"], t["C"], D=t["D"], z=t["z"], delta_bias=t["bias"],
+                           delta_softplus=True, reverse=rev, complement=comp)
+    assert relerr(to_np(out), ref_out) < 1e-4
+    out.backward(to_t(inp["dout"], cuda))
+    for name, key in (("du", "u"), ("ddelta", "delta"), ("dA", "A"), ("dB", "B"), ("dC", "C"), ("dD", "D"),
+                      ("ddelta_bias", "bias"), ("dz", "z")):
+        assert relerr(to_np(t[key].grad), ref[name]) < 1e-4, name

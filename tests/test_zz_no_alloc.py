@@ -54,7 +54,10 @@ def test_noalloc_matches_ssm_bwd_twice(cuda, bc_dtype):
     out = torch.empty(Bsz, L, D, **f32)
     states = pr.new_states()
     p = pr.params(out=out, out_stride=D, states=states)
+    fws = _workspace(p, cuda)  # the forward keeps its ordinary workspace
     assert lib.ssm_fwd(ctypes.byref(p), stream) == _lib.SSM_OK
+    torch.cuda.synchronize()
+    del fws
 
     ref_p = pr.params(states=states)
     ref = pr.grads(ref_p, dout, D)
