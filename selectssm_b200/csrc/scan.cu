@@ -198,11 +198,16 @@ static size_t round256(size_t x) { return (x + 255) & ~size_t(255); }
 struct Seg {
   int nseg, seg_chunks;
 };
-static Seg choose_segments(const Geo& g) {
+// The forward pre-pass repeats most of the forward's work, so the forward only
+// segments to reach ~384 chains; the backward pre-pass is a light adjoint-only
+// sweep, so the backward segments further, to ~2 waves of 4 CTAs per SM.
+constexpr long kFwdChainTarget = 384;
+constexpr long kBwdChainTarget = 2L * 4 * 148;
+
+static Seg choose_segments(const Geo& g, long target) {
   const int nblk = (g.L + kChunk - 1) / kChunk;
   if (nblk == 0) return {1, 1};
   const long chains = (long)((g.Dm + kTileCh - 1) / kTileCh) * g.B;
-  const long target = 384;
   int nseg = chains > 0 ? (int)((target + chains - 1) / chains) : 1;
   const int max_seg = nblk / 4;  // at least 4 chunks (64 steps) per segment
   if (nseg > max_seg) nseg = max_seg;
@@ -212,14 +217,14 @@ static Seg choose_segments(const Geo& g) {
 }
 
 static size_t fwd_ws_bytes(const Geo& g) {
-  const Seg sg = choose_segments(g);
+  const Seg sg = choose_segments(g, kFwdChainTarget);
   if (sg.nseg <= 1) return 0;
   const size_t rows = (size_t)g.B * sg.nseg * g.Dm;
   return round256(rows * kN * 4) + round256(rows * 4);
 }
 
 static size_t bwd_ws_bytes(const Geo& g) {
-  const Seg sg = choose_segments(g);
+  const Seg sg = choose_segments(g, kBwdChainTarget);
   const size_t rows = (size_t)g.B * sg.nseg * g.Dm;
   size_t n = round256(rows * kN * 4) + 2 * round256(rows * 4);
   if (g.bcbf16) n += 2 * round256((size_t)g.B * g.L * kN * 4);
@@ -258,7 +263,7 @@ static int fill_fwd_dir(const ssm_params_t* p, const Geo& g, FwdDir* d) {
   d->flags = p->flags;
   d->gate_act = p->z ? p->gate_act : SSM_ACT_NONE;
   d->has_z = p->z != nullptr;
-  const Seg sg = choose_segments(g);
+  const Seg sg = choose_segments(g, kFwdChainTarget);
   d->nseg = sg.nseg;
   d->seg_chunks = sg.seg_chunks;
   if (sg.nseg > 1) {
@@ -307,7 +312,7 @@ struct BwdWs {
 };
 
 static void carve_ws(const ssm_params_t* p, const Geo& g, char* ws, BwdWs* w) {
-  const Seg sg = choose_segments(g);
+  const Seg sg = choose_segments(g, kBwdChainTarget);
   const size_t rows = (size_t)g.B * sg.nseg * g.Dm;
   w->dA_part = reinterpret_cast<float*>(ws);
   ws += round256(rows * kN * 4);
@@ -370,7 +375,7 @@ static int fill_bwd_dir(const ssm_params_t* p, const Geo& g, const BwdWs& w, Bwd
   d->flags = p->flags;
   d->gate_act = p->z ? p->gate_act : SSM_ACT_NONE;
   d->has_z = p->z != nullptr;
-  const Seg sg = choose_segments(g);
+  const Seg sg = choose_segments(g, kBwdChainTarget);
   d->nseg = sg.nseg;
   d->seg_chunks = sg.seg_chunks;
   d->segF = w.segF;
@@ -380,7 +385,13 @@ static int fill_bwd_dir(const ssm_params_t* p, const Geo& g, const BwdWs& w, Bwd
 
 template <typename T, typename TBC>
 static int launch_bwd_t(BwdLaunch& L, int ndir, const Geo& g, cudaStream_t s) {
-  using S = BwdSmem<T, TBC>;
+  int bytes = 0;
+  for (int d = 0; d < ndir; ++d) {
+    const BwdDir& a = L.dir[d];
+    const bool mirror = a.D && (a.flags & SSM_REVERSE) && !(a.flags & SSM_ALIGNED_SKIP);
+    const BwdLayout lay(sizeof(T), sizeof(TBC), a.has_z != 0, mirror);
+    bytes = lay.bytes > bytes ? lay.bytes : bytes;
+  }
   const int nseg = L.dir[0].nseg;
   dim3 grid((g.Dm + kTileCh - 1) / kTileCh, g.B, 1);
   if (nseg > 1) {  // segment pre-pass: adjoint carried out of every segment but the first
@@ -397,11 +408,11 @@ static int launch_bwd_t(BwdLaunch& L, int ndir, const Geo& g, cudaStream_t s) {
     SSM_CUDA_CHECK(cudaGetLastError(), "launch ssm_bwd_fold_kernel");
   }
   auto kern = ssm_bwd_kernel<T, TBC>;
-  SSM_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kBytes),
+  SSM_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes),
                  "cudaFuncSetAttribute(ssm_bwd_kernel)");
   L.zdiv = nseg;
   grid.z = ndir * nseg;
-  kern<<<grid, kThreads, S::kBytes, s>>>(L);
+  kern<<<grid, kThreads, bytes, s>>>(L);
   SSM_CUDA_CHECK(cudaGetLastError(), "launch ssm_bwd_kernel");
   return SSM_OK;
 }
@@ -438,7 +449,7 @@ static int launch_finalize(const ssm_params_t* p, const Geo& g, const BwdWs& w, 
   f.dB = p->dB;
   f.dC = p->dC;
   f.bc_stride = g.bs;
-  f.prows = g.B * choose_segments(g).nseg;
+  f.prows = g.B * choose_segments(g, kBwdChainTarget).nseg;
   f.batch = g.B;
   f.L = g.L;
   f.Dm = g.Dm;

@@ -292,10 +292,8 @@ __global__ void __launch_bounds__(kThreads, 3) ssm_fwd_kernel(const __grid_const
 }
 
 // ---------------------------------------------------------------- backward
-constexpr int kHalf = kChunk / 2;
-
-// Compiler-only fence: keeps the scheduler from hoisting a whole unrolled
-// half-chunk of shared-memory loads ahead of use (which costs registers).
+// Compiler-only fence between unrolled steps: keeps the scheduler from
+// hoisting many steps' shared-memory loads ahead of use (which costs registers).
 __device__ __forceinline__ void sched_fence() { asm volatile("" ::: "memory"); }
 
 struct BwdLane {
@@ -313,114 +311,47 @@ __device__ __forceinline__ float reduce_scatter4(const BwdLane& ln, float v0, fl
   return q;
 }
 
-// Forward recurrence over steps [T0, T0+kHalf) of the staged chunk, updating h.
-// STORE keeps alpha_t and alpha_t*h_{t-1} for the reverse sweep; SIDE also
-// forms y_t = C_t.h_t (owner lanes, for dz) and the dC_t = sum_d dy_t h_t partials.
-template <int T0, bool STORE, bool SIDE, typename TBC>
-__device__ __forceinline__ void bwd_forward_half(const BwdLane& ln, float (&h)[kNL], float (&al)[kHalf][kNL],
-                                                 float (&hq)[kHalf][kNL], float (&yv)[4], const float (&dtv)[4],
-                                                 const float (&dtx)[4], const float (&dys)[4],
-                                                 const float (&An)[kNL], const TBC* sB, const TBC* sC, float* red) {
-#pragma unroll
-  for (int tl = T0; tl < T0 + kHalf; ++tl) {
-    sched_fence();
-    const int src = (ln.lane & ~3) | (tl & 3);
-    const float dt = __shfl_sync(kFull, dtv[tl >> 2], src);
-    const float dx = __shfl_sync(kFull, dtx[tl >> 2], src);
-    const float dt2 = dt * kLog2e;
-    const float4 Bv = ld4(sB + tl * kN + ln.nq * kNL);
-    const float bv[4] = {Bv.x, Bv.y, Bv.z, Bv.w};
-#pragma unroll
-    for (int k = 0; k < kNL; ++k) {
-      const float a = ex2(An[k] * dt2);
-      const float q = a * h[k];
-      h[k] = fmaf(bv[k], dx, q);
-      if (STORE) {
-        al[tl - T0][k] = a;
-        hq[tl - T0][k] = q;
-      }
-    }
-    if (SIDE) {
-      const float dy = __shfl_sync(kFull, dys[tl >> 2], src);
-      const float4 Cv = ld4(sC + tl * kN + ln.nq * kNL);
-      if (ln.has_z) {
-        float yp = Cv.x * h[0] + Cv.y * h[1] + Cv.z * h[2] + Cv.w * h[3];
-        yp += __shfl_xor_sync(kFull, yp, 1);
-        yp += __shfl_xor_sync(kFull, yp, 2);
-        if ((tl & 3) == ln.nq) yv[tl >> 2] = yp;
-      }
-      const float s = reduce_scatter4(ln, dy * h[0], dy * h[1], dy * h[2], dy * h[3]);
-      if (!ln.up2) red[(ln.warp * kChunk + tl) * 32 + kN + ln.nq * kNL + (ln.up4 ? 2 : 0) + (ln.up3 ? 1 : 0)] = s;
-    }
+// Backward shared-memory layout (bytes), sized at run time: the output-frame
+// copies of u and the scan-frame copies of dout / z only exist for the reverse
+// direction with the reference's skip frame.
+struct BwdLayout {
+  int offU, offDelta, offDo, offZo, offUo, offDs, offZs, offB, offC, offS, stage;
+  int offRed, offBars, offTmem, bytes;
+  __host__ __device__ BwdLayout(int es, int esbc, bool has_z, bool need_mirror) {
+    const int act = kChunk * kTileCh * es, bc = kChunk * kN * esbc;
+    int o = 0;
+    offU = o; o += act;
+    offDelta = o; o += act;
+    offDo = o; o += act;
+    offZo = o; if (has_z) o += act;
+    offUo = o; if (need_mirror) o += act;
+    offDs = o; if (need_mirror) o += act;
+    offZs = o; if (need_mirror && has_z) o += act;
+    offB = o; o += bc;
+    offC = o; o += bc;
+    offS = o; o += kTileCh * kN * 4;     // chunk-start state tile (fp32)
+    stage = (o + 127) & ~127;
+    offRed = stage * kBwdStages;          // two dB/dC partial buffers
+    offBars = offRed + 2 * kWarps * kChunk * 32 * 4;
+    offTmem = offBars + 8 * kBwdStages;
+    bytes = offTmem + 16;
   }
-}
-
-// Adjoint sweep over steps T0+kHalf-1 .. T0: f_t = C_t dy_t + f_{t+1} alpha_{t+1}
-// (fa carries f alpha), with the leaf gradients of ssmrecscan.py:154-160.
-template <int T0, typename TBC, typename T>
-__device__ __forceinline__ void bwd_reverse_half(const BwdLane& ln, const float (&al)[kHalf][kNL],
-                                                 const float (&hq)[kHalf][kNL], float (&fa)[kNL], float (&dA)[kNL],
-                                                 const float (&dtv)[4], const float (&dtx)[4], const float (&dys)[4],
-                                                 const float (&An)[kNL], const TBC* sB, const TBC* sC,
-                                                 const T* su_col, float* red, float (&dxs)[4], float (&ddt)[4]) {
-#pragma unroll
-  for (int tl = T0 + kHalf - 1; tl >= T0; --tl) {
-    sched_fence();
-    const int src = (ln.lane & ~3) | (tl & 3);
-    const float dt = __shfl_sync(kFull, dtv[tl >> 2], src);
-    const float dx = __shfl_sync(kFull, dtx[tl >> 2], src);
-    const float dy = __shfl_sync(kFull, dys[tl >> 2], src);
-    const float4 Bv = ld4(sB + tl * kN + ln.nq * kNL);
-    const float4 Cv = ld4(sC + tl * kN + ln.nq * kNL);
-    const float bv[4] = {Bv.x, Bv.y, Bv.z, Bv.w};
-    const float cv[4] = {Cv.x, Cv.y, Cv.z, Cv.w};
-    float sAw = 0.f, sBf = 0.f, vB[kNL];
-#pragma unroll
-    for (int k = 0; k < kNL; ++k) {
-      const float f = fmaf(cv[k], dy, fa[k]);
-      const float w = f * hq[tl - T0][k];
-      dA[k] = fmaf(dt, w, dA[k]);
-      sAw = fmaf(An[k], w, sAw);
-      sBf = fmaf(bv[k], f, sBf);
-      vB[k] = dx * f;
-      fa[k] = f * al[tl - T0][k];
-    }
-    sAw += __shfl_xor_sync(kFull, sAw, 1);
-    sBf += __shfl_xor_sync(kFull, sBf, 1);
-    sAw += __shfl_xor_sync(kFull, sAw, 2);
-    sBf += __shfl_xor_sync(kFull, sBf, 2);
-    if ((tl & 3) == ln.nq) {
-      dxs[tl >> 2] = dt * sBf;
-      ddt[tl >> 2] = fmaf(ld_f(su_col + tl * kTileCh), sBf, sAw);  // x sum_n B f + sum_n A w
-    }
-    const float s = reduce_scatter4(ln, vB[0], vB[1], vB[2], vB[3]);
-    if (!ln.up2) red[(ln.warp * kChunk + tl) * 32 + ln.nq * kNL + (ln.up4 ? 2 : 0) + (ln.up3 ? 1 : 0)] = s;
+  // bytes one stage's TMA loads deliver (the start state only when j > 0)
+  __host__ __device__ uint32_t tx(int es, int esbc, bool has_z, bool need_mirror, bool with_state) const {
+    const int act = kChunk * kTileCh * es, bc = kChunk * kN * esbc;
+    return 3 * act + 2 * bc + (has_z ? act : 0) + (need_mirror ? (has_z ? 3 : 2) * act : 0) +
+           (with_state ? kTileCh * kN * 4 : 0);
   }
-}
-
-template <typename T, typename TBC>
-struct BwdSmem {
-  static constexpr int kAct = kChunk * kTileCh * (int)sizeof(T);
-  static constexpr int kBC = kChunk * kN * (int)sizeof(TBC);
-  static constexpr int kSt = kTileCh * kN * 4;  // chunk-start state tile (fp32)
-  static constexpr int kOffU = 0, kOffDelta = kAct, kOffZo = 2 * kAct, kOffDo = 3 * kAct, kOffUo = 4 * kAct,
-                       kOffZs = 5 * kAct, kOffDs = 6 * kAct;
-  static constexpr int kOffB = 7 * kAct, kOffC = 7 * kAct + kBC, kOffS = 7 * kAct + 2 * kBC;
-  static constexpr int kStage = 7 * kAct + 2 * kBC + kSt;
-  static constexpr int kRed = kWarps * kChunk * 32 * 4;  // one dB/dC partial buffer
-  static constexpr int kOffRed = kStage * kBwdStages;
-  static constexpr int kBars = kOffRed + 2 * kRed;
-  static constexpr int kBytes = kBars + 8 * kBwdStages;
 };
 
+// TMEM columns per CTA: 16 steps x (4 alpha + 4 alpha*h) per lane.
+constexpr uint32_t kBwdTmemCols = kChunk * 2 * kNL;
+
 template <typename T, typename TBC>
-__global__ void __launch_bounds__(kThreads, 3) ssm_bwd_kernel(const __grid_constant__ BwdLaunch P) {
-  using S = BwdSmem<T, TBC>;
+__global__ void __launch_bounds__(kThreads, 4) ssm_bwd_kernel(const __grid_constant__ BwdLaunch P) {
   const BwdDir& a = P.dir[blockIdx.z / P.zdiv];
   const int seg = blockIdx.z % P.zdiv;
   extern __shared__ __align__(1024) unsigned char smem[];
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::kBars);
-  float* sRed = reinterpret_cast<float*>(smem + S::kOffRed);
 
   const int b = blockIdx.y;
   const int c0 = blockIdx.x * kTileCh;
@@ -435,43 +366,49 @@ __global__ void __launch_bounds__(kThreads, 3) ssm_bwd_kernel(const __grid_const
   const bool aligned = (a.flags & SSM_ALIGNED_SKIP) != 0;
   const bool softplus = (a.flags & SSM_DELTA_SOFTPLUS) != 0;
   const bool has_z = a.has_z != 0, has_D = a.D != nullptr;
-  const bool need_uo = has_D && rev && !aligned;   // skip u at output-frame coordinates
-  const bool need_s = has_D && rev && !aligned;    // dout/z at scan coordinates (skip grad)
+  const bool mirror = has_D && rev && !aligned;  // skip frame of the reverse direction
   const int nblk = (L + kChunk - 1) / kChunk;
   const int j1 = min(nblk, (seg + 1) * a.seg_chunks);
   const int nloc = j1 - seg * a.seg_chunks;
   const bool cvalid = c < Dm;
   const int co = comp ? Dm - 1 - c : c;
   const int oc0 = comp ? Dm - kTileCh - c0 : c0;
+  const BwdLayout S(sizeof(T), sizeof(TBC), has_z, mirror);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S.offBars);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + S.offTmem);
+  float* sRed = reinterpret_cast<float*>(smem + S.offRed);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kBwdStages; ++s) mbar_init(&bars[s], 1);
     fence_mbar_init();
   }
+  if (warp == 0) tmem_alloc(tmem_slot, kBwdTmemCols);
+  tmem_fence_before_sync();
   __syncthreads();
+  tmem_fence_after_sync();
+  const uint32_t tbase = *tmem_slot;
+  const uint32_t trow = tbase + ((uint32_t)(warp * 32) << 16);  // this warp's lane quarter
 
-  const uint32_t tx_base = 3 * S::kAct + 2 * S::kBC + (has_z ? S::kAct : 0) + (need_uo ? S::kAct : 0) +
-                           (need_s ? (has_z ? 2 : 1) * S::kAct : 0);
   // it-th issue loads chunk j = j1-1-it (the segment's chunks, last first)
   auto issue = [&](int it) {
     const int j = j1 - 1 - it;
-    unsigned char* st = smem + (it % kBwdStages) * S::kStage;
+    unsigned char* st = smem + (it % kBwdStages) * S.stage;
     uint64_t* bar = &bars[it % kBwdStages];
     const int t0 = j * kChunk;
     const int ot0 = rev ? L - kChunk - t0 : t0;
-    mbar_arrive_expect_tx(bar, tx_base + (j > 0 ? S::kSt : 0));
-    tma_load_3d(st + S::kOffU, &a.tm_u, bar, c0, t0, b);
-    tma_load_3d(st + S::kOffDelta, &a.tm_delta, bar, c0, t0, b);
-    tma_load_3d(st + S::kOffB, &a.tm_B, bar, 0, t0, b);
-    tma_load_3d(st + S::kOffC, &a.tm_C, bar, 0, t0, b);
-    tma_load_3d(st + S::kOffDo, &a.tm_dout, bar, oc0, ot0, b);
-    if (has_z) tma_load_3d(st + S::kOffZo, &a.tm_z, bar, oc0, ot0, b);
-    if (need_uo) tma_load_3d(st + S::kOffUo, &a.tm_u, bar, oc0, ot0, b);
-    if (need_s) {
-      tma_load_3d(st + S::kOffDs, &a.tm_dout, bar, c0, t0, b);
-      if (has_z) tma_load_3d(st + S::kOffZs, &a.tm_z, bar, c0, t0, b);
+    mbar_arrive_expect_tx(bar, S.tx(sizeof(T), sizeof(TBC), has_z, mirror, j > 0));
+    tma_load_3d(st + S.offU, &a.tm_u, bar, c0, t0, b);
+    tma_load_3d(st + S.offDelta, &a.tm_delta, bar, c0, t0, b);
+    tma_load_3d(st + S.offB, &a.tm_B, bar, 0, t0, b);
+    tma_load_3d(st + S.offC, &a.tm_C, bar, 0, t0, b);
+    tma_load_3d(st + S.offDo, &a.tm_dout, bar, oc0, ot0, b);
+    if (has_z) tma_load_3d(st + S.offZo, &a.tm_z, bar, oc0, ot0, b);
+    if (mirror) {
+      tma_load_3d(st + S.offUo, &a.tm_u, bar, oc0, ot0, b);
+      tma_load_3d(st + S.offDs, &a.tm_dout, bar, c0, t0, b);
+      if (has_z) tma_load_3d(st + S.offZs, &a.tm_z, bar, c0, t0, b);
     }
-    if (j > 0) tma_load_3d(st + S::kOffS, &a.tm_states, bar, 0, c0, b * nblk + j - 1);
+    if (j > 0) tma_load_3d(st + S.offS, &a.tm_states, bar, 0, c0, b * nblk + j - 1);
   };
   if (threadIdx.x == 0) {
     const int npre = nloc < kBwdStages ? nloc : kBwdStages;
@@ -494,30 +431,33 @@ __global__ void __launch_bounds__(kThreads, 3) ssm_bwd_kernel(const __grid_const
   T* du_g = reinterpret_cast<T*>(a.du);
   T* dd_g = reinterpret_cast<T*>(a.ddelta);
   T* dz_g = reinterpret_cast<T*>(a.dz);
-  const bool up4 = (lane & 16) != 0, up3 = (lane & 8) != 0, up2 = (lane & 4) != 0;
+  const BwdLane ln{lane, nq, warp, (lane & 16) != 0, (lane & 8) != 0, (lane & 4) != 0, has_z};
+  const int red_n = nq * kNL + (ln.up4 ? 2 : 0) + (ln.up3 ? 1 : 0);
+  bool failed = false;
 
   for (int it = 0; it < nloc; ++it) {
     const int j = j1 - 1 - it;
     const int s = it % kBwdStages;
     const bool ok = mbar_wait_bounded(&bars[s], (it / kBwdStages) & 1);
     if (!__syncthreads_and(ok)) {
-      if (threadIdx.x == 0) report(a.status, kStatusTimeout);
-      return;
+      failed = true;
+      break;
     }
-    const unsigned char* st = smem + s * S::kStage;
-    const T* su = reinterpret_cast<const T*>(st + S::kOffU);
-    const T* sd = reinterpret_cast<const T*>(st + S::kOffDelta);
-    const T* szo = reinterpret_cast<const T*>(st + S::kOffZo);
-    const T* sdo = reinterpret_cast<const T*>(st + S::kOffDo);
-    const T* suo = reinterpret_cast<const T*>(st + S::kOffUo);
-    const T* szs = reinterpret_cast<const T*>(st + S::kOffZs);
-    const T* sds = reinterpret_cast<const T*>(st + S::kOffDs);
-    const TBC* sB = reinterpret_cast<const TBC*>(st + S::kOffB);
-    const TBC* sC = reinterpret_cast<const TBC*>(st + S::kOffC);
-    const float* sS = reinterpret_cast<const float*>(st + S::kOffS);
+    const unsigned char* st = smem + s * S.stage;
+    const T* su = reinterpret_cast<const T*>(st + S.offU);
+    const T* sd = reinterpret_cast<const T*>(st + S.offDelta);
+    const T* szo = reinterpret_cast<const T*>(st + S.offZo);
+    const T* sdo = reinterpret_cast<const T*>(st + S.offDo);
+    const T* suo = reinterpret_cast<const T*>(st + S.offUo);
+    const T* szs = reinterpret_cast<const T*>(st + S.offZs);
+    const T* sds = reinterpret_cast<const T*>(st + S.offDs);
+    const TBC* sB = reinterpret_cast<const TBC*>(st + S.offB);
+    const TBC* sC = reinterpret_cast<const TBC*>(st + S.offC);
+    const float* sS = reinterpret_cast<const float*>(st + S.offS);
     float* red = sRed + (it & 1) * (kWarps * kChunk * 32);
+    const int col = comp ? kTileCh - 1 - cl : cl;
 
-    // ---- per-step scalars for the lane's 4 steps
+    // ---- per-step scalars for the lane's 4 steps (tl = nq + 4i)
     float dtv[4], dtx[4], dys[4];
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
@@ -530,29 +470,52 @@ __global__ void __launch_bounds__(kThreads, 3) ssm_bwd_kernel(const __grid_const
       dtv[i] = dt;
       dtx[i] = valid ? dt * x : 0.f;
       const int row = rev ? kChunk - 1 - tl : tl;
-      const int col = comp ? kTileCh - 1 - cl : cl;
       float g = ld_f(sdo + row * kTileCh + col);
       if (has_z) g *= act_f(ld_f(szo + row * kTileCh + col), a.gate_act);
       dys[i] = valid ? g : 0.f;
     }
 
-    // ---- chunk start state
-    float hs[kNL];
+    // ---- forward recompute from the chunk-start state; alpha_t and
+    // alpha_t h_{t-1} of every step go to TMEM (columns 8 tl .. 8 tl + 7)
+    float h[kNL];
     if (j > 0) {
       const float4 h0 = *reinterpret_cast<const float4*>(sS + cl * kN + nq * kNL);
-      hs[0] = h0.x; hs[1] = h0.y; hs[2] = h0.z; hs[3] = h0.w;
+      h[0] = h0.x; h[1] = h0.y; h[2] = h0.z; h[3] = h0.w;
     } else {
-      hs[0] = hs[1] = hs[2] = hs[3] = 0.f;
+      h[0] = h[1] = h[2] = h[3] = 0.f;
     }
-    // Registers hold alpha and alpha*h_{t-1} for half a chunk (8 steps).  The
-    // second half is recomputed from the mid-chunk state and swept first; the
-    // first half is then recomputed from the chunk start and swept.
-    float h[kNL] = {hs[0], hs[1], hs[2], hs[3]};
-    float al[kHalf][kNL], hq[kHalf][kNL];
     float yv[4] = {0.f, 0.f, 0.f, 0.f};
-    const BwdLane ln{lane, nq, warp, up4, up3, up2, has_z};
-    bwd_forward_half<0, false, true>(ln, h, al, hq, yv, dtv, dtx, dys, An, sB, sC, red);
-    bwd_forward_half<kHalf, true, true>(ln, h, al, hq, yv, dtv, dtx, dys, An, sB, sC, red);
+#pragma unroll
+    for (int tl = 0; tl < kChunk; ++tl) {
+      sched_fence();
+      const int src = (lane & ~3) | (tl & 3);
+      const float dt = __shfl_sync(kFull, dtv[tl >> 2], src);
+      const float dx = __shfl_sync(kFull, dtx[tl >> 2], src);
+      const float dy = __shfl_sync(kFull, dys[tl >> 2], src);
+      const float dt2 = dt * kLog2e;
+      const float4 Bv = ld4(sB + tl * kN + nq * kNL);
+      const float4 Cv = ld4(sC + tl * kN + nq * kNL);
+      const float bv[4] = {Bv.x, Bv.y, Bv.z, Bv.w};
+      float keep[8];
+#pragma unroll
+      for (int k = 0; k < kNL; ++k) {
+        const float al = ex2(An[k] * dt2);
+        const float q = al * h[k];
+        h[k] = fmaf(bv[k], dx, q);
+        keep[k] = al;
+        keep[4 + k] = q;
+      }
+      tmem_st8(trow + tl * 8, keep);
+      if (has_z) {
+        float yp = Cv.x * h[0] + Cv.y * h[1] + Cv.z * h[2] + Cv.w * h[3];
+        yp += __shfl_xor_sync(kFull, yp, 1);
+        yp += __shfl_xor_sync(kFull, yp, 2);
+        if ((tl & 3) == nq) yv[tl >> 2] = yp;
+      }
+      const float sc = reduce_scatter4(ln, dy * h[0], dy * h[1], dy * h[2], dy * h[3]);
+      if (!ln.up2) red[(warp * kChunk + tl) * 32 + kN + red_n] = sc;
+    }
+    tmem_wait_st();
 
     // ---- dz (needs the recomputed pre-gate output)
     if (has_z) {
@@ -562,13 +525,9 @@ __global__ void __launch_bounds__(kThreads, 3) ssm_bwd_kernel(const __grid_const
         const int t = j * kChunk + tl;
         if (t < L && cvalid) {
           const int row = rev ? kChunk - 1 - tl : tl;
-          const int col = comp ? kTileCh - 1 - cl : cl;
           const int l = rev ? L - 1 - t : t;
           float pre = yv[i];
-          if (has_D) {
-            const float xs = need_uo ? ld_f(suo + row * kTileCh + col) : ld_f(su + tl * kTileCh + cl);
-            pre = fmaf(Dso, xs, pre);
-          }
+          if (has_D) pre = fmaf(Dso, mirror ? ld_f(suo + row * kTileCh + col) : ld_f(su + tl * kTileCh + cl), pre);
           const float zz = ld_f(szo + row * kTileCh + col);
           const float g = ld_f(sdo + row * kTileCh + col) * pre * act_grad_f(zz, a.gate_act);
           st_act(dz_g + ((size_t)b * L + l) * a.z_stride + co, g);
@@ -576,12 +535,52 @@ __global__ void __launch_bounds__(kThreads, 3) ssm_bwd_kernel(const __grid_const
       }
     }
 
-    // ---- reverse sweeps
+    // ---- adjoint sweep, steps 15..0, two steps per TMEM load
     float dxs[4], ddt[4];
-    bwd_reverse_half<kHalf>(ln, al, hq, fa, dA, dtv, dtx, dys, An, sB, sC, su + cl, red, dxs, ddt);
-    h[0] = hs[0]; h[1] = hs[1]; h[2] = hs[2]; h[3] = hs[3];
-    bwd_forward_half<0, true, false>(ln, h, al, hq, yv, dtv, dtx, dys, An, sB, sC, red);
-    bwd_reverse_half<0>(ln, al, hq, fa, dA, dtv, dtx, dys, An, sB, sC, su + cl, red, dxs, ddt);
+    uint32_t buf[2][16];  // alternating step-pair buffers (static indices once unrolled)
+    tmem_ld16(trow + (kChunk - 2) * 8, buf[(kChunk / 2 - 1) & 1]);
+    tmem_wait_ld();
+#pragma unroll
+    for (int pr = kChunk / 2 - 1; pr >= 0; --pr) {
+      if (pr > 0) tmem_ld16(trow + (2 * pr - 2) * 8, buf[(pr - 1) & 1]);
+#pragma unroll
+      for (int half = 1; half >= 0; --half) {
+        const int tl = 2 * pr + half;
+        sched_fence();
+        const int src = (lane & ~3) | (tl & 3);
+        const float dt = __shfl_sync(kFull, dtv[tl >> 2], src);
+        const float dx = __shfl_sync(kFull, dtx[tl >> 2], src);
+        const float dy = __shfl_sync(kFull, dys[tl >> 2], src);
+        const float4 Bv = ld4(sB + tl * kN + nq * kNL);
+        const float4 Cv = ld4(sC + tl * kN + nq * kNL);
+        const float bv[4] = {Bv.x, Bv.y, Bv.z, Bv.w};
+        const float cv[4] = {Cv.x, Cv.y, Cv.z, Cv.w};
+        float sAw = 0.f, sBf = 0.f, vB[kNL];
+#pragma unroll
+        for (int k = 0; k < kNL; ++k) {
+          const float al = __uint_as_float(buf[pr & 1][half * 8 + k]);
+          const float q = __uint_as_float(buf[pr & 1][half * 8 + 4 + k]);
+          const float f = fmaf(cv[k], dy, fa[k]);
+          const float w = f * q;
+          dA[k] = fmaf(dt, w, dA[k]);
+          sAw = fmaf(An[k], w, sAw);
+          sBf = fmaf(bv[k], f, sBf);
+          vB[k] = dx * f;
+          fa[k] = f * al;
+        }
+        sAw += __shfl_xor_sync(kFull, sAw, 1);
+        sBf += __shfl_xor_sync(kFull, sBf, 1);
+        sAw += __shfl_xor_sync(kFull, sAw, 2);
+        sBf += __shfl_xor_sync(kFull, sBf, 2);
+        if ((tl & 3) == nq) {
+          dxs[tl >> 2] = dt * sBf;
+          ddt[tl >> 2] = fmaf(ld_f(su + tl * kTileCh + cl), sBf, sAw);  // x sum_n B f + sum_n A w
+        }
+        const float sb = reduce_scatter4(ln, vB[0], vB[1], vB[2], vB[3]);
+        if (!ln.up2) red[(warp * kChunk + tl) * 32 + red_n] = sb;
+      }
+      if (pr > 0) tmem_wait_ld();
+    }
 
     // ---- epilogue: du, ddelta, skip grads
 #pragma unroll
@@ -593,7 +592,7 @@ __global__ void __launch_bounds__(kThreads, 3) ssm_bwd_kernel(const __grid_const
         float du = dxs[i];
         if (has_D) {
           float sg = dys[i];
-          if (need_s) {
+          if (mirror) {
             sg = ld_f(sds + tl * kTileCh + cl);
             if (has_z) sg *= act_f(ld_f(szs + tl * kTileCh + cl), a.gate_act);
           }
@@ -631,13 +630,22 @@ __global__ void __launch_bounds__(kThreads, 3) ssm_bwd_kernel(const __grid_const
     }
   }
 
-  // per-(batch row, channel) partials of the parameter gradients
+  // release TMEM (every thread's accesses are complete)
+  tmem_fence_before_sync();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tbase, kBwdTmemCols);
+  if (failed) {
+    if (threadIdx.x == 0) report(a.status, kStatusTimeout);
+    return;
+  }
+
+  // per-(batch row, segment, channel) partials of the parameter gradients
   dD_acc += __shfl_xor_sync(kFull, dD_acc, 1);
   dD_acc += __shfl_xor_sync(kFull, dD_acc, 2);
   db_acc += __shfl_xor_sync(kFull, db_acc, 1);
   db_acc += __shfl_xor_sync(kFull, db_acc, 2);
   if (cvalid) {
-    const size_t r = (size_t)b * a.nseg + blockIdx.z % P.zdiv;
+    const size_t r = (size_t)b * a.nseg + seg;
     *reinterpret_cast<float4*>(a.dA_part + (r * Dm + c) * kN + nq * kNL) = make_float4(dA[0], dA[1], dA[2], dA[3]);
     if (nq == 0) {
       a.dD_part[r * Dm + c] = dD_acc;
