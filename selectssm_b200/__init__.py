@@ -17,3 +17,4 @@ from .ops import (  # noqa: F401
 )
 
 __version__ = "0.1.0"
+from .modules import BidirectionalMamba, SelectiveSSM  # noqa: F401,E402
