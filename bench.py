@@ -238,6 +238,7 @@ def main():
     import torch.distributed as dist
     import selectssm_b200 as S
     from selectssm_b200 import _lib
+    from selectssm_b200.parallel import allreduce_grads
 
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
@@ -257,9 +258,8 @@ def main():
         out = S.selective_scan(inputs["u"], inputs["delta"], inputs["A"], inputs["B"], inputs["C"], D=inputs["D"],
                                z=inputs["z"], delta_softplus=True)
         out.backward(inputs["dout"])
-        if world > 1:
-            flat = torch.cat([inputs["A"].grad.reshape(-1), inputs["D"].grad.reshape(-1)])
-            dist.all_reduce(flat)
+        if world > 1:  # batch sharding: one all-reduce of the parameter gradients
+            allreduce_grads([inputs["A"], inputs["D"]])
         return out
 
     for _ in range(max(3, args.warmup)):

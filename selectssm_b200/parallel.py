@@ -1,0 +1,100 @@
+"""Multi-GPU partitioning of the scan: one process per GPU over torch.distributed.
+
+The reference has no multi-device code; the partition follows from the math of
+the recurrence (each (batch row, channel) is an independent scan; B and C are
+shared by all channels of a batch row):
+
+* Batch sharding (``shard_batch``): every rank scans its own batch rows with no
+  communication in the forward.  The backward produces per-rank partial sums of
+  the parameter gradients (A / A_log, D, dt bias, and the projections around the
+  scan); ``allreduce_grads`` sums them with ONE all-reduce of a flattened buffer.
+* Channel (d_inner) sharding (``shard_channels`` + ``replicated_bc``): every rank
+  scans a contiguous slice of channels with B and C replicated.  dA, dD and the
+  dt-bias gradient are per channel and stay local, but dB and dC are sums over
+  all channels (src/selectssm/ssmrecscan.py:158-159), so their gradient is
+  all-reduced in the backward -- ``replicated_bc`` inserts that reduction.
+
+Collectives use whatever backend the default process group has (NCCL over
+NVLink on the B200 box; gloo in the CPU tests).
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+
+def world():
+    """(rank, world_size) of the default group, or (0, 1) when not initialised."""
+    if dist.is_available() and dist.is_initialized():
+        return dist.get_rank(), dist.get_world_size()
+    return 0, 1
+
+
+def shard_range(n: int, rank: int, world_size: int):
+    """Contiguous [start, stop) of n items owned by rank (sizes differ by at most 1)."""
+    base, extra = divmod(n, world_size)
+    start = rank * base + min(rank, extra)
+    return start, start + base + (1 if rank < extra else 0)
+
+
+def shard_batch(x: torch.Tensor, rank: int = None, world_size: int = None) -> torch.Tensor:
+    """This rank's batch rows of a (B, ...) tensor."""
+    r, w = world()
+    rank = r if rank is None else rank
+    world_size = w if world_size is None else world_size
+    s, e = shard_range(x.shape[0], rank, world_size)
+    return x[s:e]
+
+
+def shard_channels(x: torch.Tensor, rank: int = None, world_size: int = None, dim: int = -1,
+                   multiple: int = 8) -> torch.Tensor:
+    """This rank's channel slice along ``dim``; slices are kept at multiples of
+    ``multiple`` channels (the kernels need 16-byte aligned channel rows)."""
+    r, w = world()
+    rank = r if rank is None else rank
+    world_size = w if world_size is None else world_size
+    n = x.shape[dim]
+    if n % multiple:
+        raise ValueError(f"channel count {n} is not a multiple of {multiple}")
+    s, e = shard_range(n // multiple, rank, world_size)
+    return x.narrow(dim, s * multiple, (e - s) * multiple)
+
+
+class _SumGradAcrossRanks(torch.autograd.Function):
+    """Identity forward; the backward all-reduces (sums) the incoming gradient."""
+
+    @staticmethod
+    def forward(ctx, x, group):
+        ctx.group = group
+        return x.view_as(x)
+
+    @staticmethod
+    def backward(ctx, g):
+        g = g.contiguous()
+        if dist.is_initialized():
+            dist.all_reduce(g, op=dist.ReduceOp.SUM, group=ctx.group)
+        return g, None
+
+
+def replicated_bc(Bm: torch.Tensor, Cm: torch.Tensor, group=None):
+    """Mark B and C as replicated across a channel-sharded group: the gradients
+    each rank computes from its channels are summed over ranks."""
+    return _SumGradAcrossRanks.apply(Bm, group), _SumGradAcrossRanks.apply(Cm, group)
+
+
+def allreduce_grads(params, group=None, average: bool = False):
+    """Sum (or average) the .grad of ``params`` over ranks with a single
+    all-reduce of one flattened buffer (batch sharding)."""
+    ps = [p for p in params if p.grad is not None]
+    if not ps or not dist.is_initialized():
+        return
+    flat = torch.cat([p.grad.reshape(-1) for p in ps])
+    dist.all_reduce(flat, op=dist.ReduceOp.SUM, group=group)
+    if average:
+        flat /= dist.get_world_size(group)
+    off = 0
+    for p in ps:
+        n = p.grad.numel()
+        p.grad.copy_(flat[off:off + n].view_as(p.grad))
+        off += n
