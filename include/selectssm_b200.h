@@ -73,10 +73,10 @@ enum ssm_flags {
 
 enum ssm_act { SSM_ACT_NONE = 0, SSM_ACT_SILU = 1, SSM_ACT_GELU = 2, SSM_ACT_RELU = 3 };
 
-/* Scan chunk (forward checkpoint) length in steps.  The forward writes the
- * state h (fp32, dstate values per channel) after every SSM_CHUNK steps; the
- * backward restarts from those states. */
-#define SSM_CHUNK 16
+/* Checkpoint spacing in steps.  The forward writes the state h (fp32, dstate
+ * values per channel) after every SSM_CHUNK steps; the backward restarts from
+ * those states. */
+#define SSM_CHUNK 8
 
 typedef struct ssm_params {
   int32_t batch, seqlen, dim, dstate;   /* B, L, D, N (N must be 16) */
@@ -102,7 +102,7 @@ typedef struct ssm_params {
   const void* z;                        /* (B,L,D) gate input, output frame; NULL: no gate */
   /* ---- forward outputs ---- */
   void* out;                            /* (B,L,D) output frame                          */
-  float* states;                        /* (B, ceil(L/16), D, N) fp32 state after each chunk;
+  float* states;                        /* (B, ceil(L/8), D, N) fp32 state after every 8 steps;
                                            written by ssm_fwd, read by ssm_bwd            */
   /* ---- backward ---- */
   const void* dout;                     /* (B,L,D) output frame                          */
@@ -123,7 +123,7 @@ typedef struct ssm_params {
 
 /* Bytes of scratch the backward needs for these params (the forward needs none). */
 SSM_API size_t ssm_workspace_bytes(const ssm_params_t* p);
-/* Number of floats of p->states: B * ceil(L/16) * D * N. */
+/* Number of floats of p->states: B * ceil(L/8) * D * N. */
 SSM_API size_t ssm_states_elems(const ssm_params_t* p);
 
 /* Forward (see top of file).  Writes out and states. */

@@ -33,7 +33,7 @@ SSM_ALIGNED_SKIP = 1 << 3
 
 ACT_CODES = {None: 0, "none": 0, "silu": 1, "gelu": 2, "relu": 3}
 
-SSM_CHUNK = 16
+SSM_CHUNK = 8
 NOALLOC_SCRATCH_BYTES = 8 << 20
 DSTATE = 16
 

@@ -11,7 +11,8 @@
 
 namespace ssm {
 
-constexpr int kChunk = 16;        // steps per chunk == checkpoint spacing
+constexpr int kChunk = 16;        // steps per TMA stage
+constexpr int kCk = 8;            // forward checkpoint spacing (backward register block)
 constexpr int kN = 16;            // state size supported by this build
 constexpr int kNL = 4;            // states owned by one lane
 constexpr int kLanesPerCh = kN / kNL;          // 4 lanes share one channel
@@ -184,6 +185,36 @@ __device__ __forceinline__ float act_grad_f(float x, int act) {
     default: return 1.f;
   }
 }
+
+// ---------------------------------------------------------------- packed fp32 (sm_100 f32x2)
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+__device__ __forceinline__ float2 fmul2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "mul.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+__device__ __forceinline__ float2 dup2(float v) { return make_float2(v, v); }
 
 // ---------------------------------------------------------------- dtype helpers
 template <typename T> struct Cvt;

@@ -4,7 +4,7 @@
 #include <cstring>
 #include <mutex>
 
-#include "scan_kernels.cuh"
+#include "scan_bwd.cuh"
 
 namespace ssm {
 
@@ -201,13 +201,20 @@ struct Seg {
 // The forward pre-pass repeats most of the forward's work, so the forward only
 // segments to reach ~384 chains; the backward pre-pass is a light adjoint-only
 // sweep, so the backward segments further, to ~2 waves of 4 CTAs per SM.
-constexpr long kFwdChainTarget = 384;
-constexpr long kBwdChainTarget = 2L * 4 * 148;
+// Targets count CTAs: the forward's 32-channel CTAs and the backward's
+// 128-channel CTAs (2 resident per SM: aim at 2 waves).
+struct SegPolicy {
+  long target;
+  int tile;
+};
+constexpr SegPolicy kFwdSeg{384, kTileCh};
+constexpr SegPolicy kBwdSeg{2L * 2 * 148, kBTile};
 
-static Seg choose_segments(const Geo& g, long target) {
+static Seg choose_segments(const Geo& g, SegPolicy pol) {
+  const long target = pol.target;
   const int nblk = (g.L + kChunk - 1) / kChunk;
   if (nblk == 0) return {1, 1};
-  const long chains = (long)((g.Dm + kTileCh - 1) / kTileCh) * g.B;
+  const long chains = (long)((g.Dm + pol.tile - 1) / pol.tile) * g.B;
   int nseg = chains > 0 ? (int)((target + chains - 1) / chains) : 1;
   const int max_seg = nblk / 4;  // at least 4 chunks (64 steps) per segment
   if (nseg > max_seg) nseg = max_seg;
@@ -217,14 +224,14 @@ static Seg choose_segments(const Geo& g, long target) {
 }
 
 static size_t fwd_ws_bytes(const Geo& g) {
-  const Seg sg = choose_segments(g, kFwdChainTarget);
+  const Seg sg = choose_segments(g, kFwdSeg);
   if (sg.nseg <= 1) return 0;
   const size_t rows = (size_t)g.B * sg.nseg * g.Dm;
   return round256(rows * kN * 4) + round256(rows * 4);
 }
 
 static size_t bwd_ws_bytes(const Geo& g) {
-  const Seg sg = choose_segments(g, kBwdChainTarget);
+  const Seg sg = choose_segments(g, kBwdSeg);
   const size_t rows = (size_t)g.B * sg.nseg * g.Dm;
   size_t n = round256(rows * kN * 4) + 2 * round256(rows * 4);
   if (g.bcbf16) n += 2 * round256((size_t)g.B * g.L * kN * 4);
@@ -263,7 +270,7 @@ static int fill_fwd_dir(const ssm_params_t* p, const Geo& g, FwdDir* d) {
   d->flags = p->flags;
   d->gate_act = p->z ? p->gate_act : SSM_ACT_NONE;
   d->has_z = p->z != nullptr;
-  const Seg sg = choose_segments(g, kFwdChainTarget);
+  const Seg sg = choose_segments(g, kFwdSeg);
   d->nseg = sg.nseg;
   d->seg_chunks = sg.seg_chunks;
   if (sg.nseg > 1) {
@@ -312,7 +319,7 @@ struct BwdWs {
 };
 
 static void carve_ws(const ssm_params_t* p, const Geo& g, char* ws, BwdWs* w) {
-  const Seg sg = choose_segments(g, kBwdChainTarget);
+  const Seg sg = choose_segments(g, kBwdSeg);
   const size_t rows = (size_t)g.B * sg.nseg * g.Dm;
   w->dA_part = reinterpret_cast<float*>(ws);
   ws += round256(rows * kN * 4);
@@ -341,21 +348,20 @@ static void carve_ws(const ssm_params_t* p, const Geo& g, char* ws, BwdWs* w) {
 
 static int fill_bwd_dir(const ssm_params_t* p, const Geo& g, const BwdWs& w, BwdDir* d) {
   const uint64_t es = g.es, eb = g.esbc;
-  bool ok = make_map(&d->tm_u, p->u, g.bf16, g.Dm, g.L, g.B, g.Dm * es, (uint64_t)g.L * g.Dm * es, kTileCh, kChunk);
+  bool ok = make_map(&d->tm_u, p->u, g.bf16, g.Dm, g.L, g.B, g.Dm * es, (uint64_t)g.L * g.Dm * es, kBTile, kChunk);
   ok = ok && make_map(&d->tm_delta, p->delta, g.bf16, g.Dm, g.L, g.B, g.Dm * es, (uint64_t)g.L * g.Dm * es,
-                      kTileCh, kChunk);
+                      kBTile, kChunk);
   ok = ok && make_map(&d->tm_B, p->Bm, g.bcbf16, kN, g.L, g.B, g.bs * eb, (uint64_t)g.L * g.bs * eb, kN, kChunk);
   ok = ok && make_map(&d->tm_C, p->Cm, g.bcbf16, kN, g.L, g.B, g.bs * eb, (uint64_t)g.L * g.bs * eb, kN, kChunk);
-  ok = ok && make_map(&d->tm_dout, p->dout, g.bf16, g.Dm, g.L, g.B, g.os * es, (uint64_t)g.L * g.os * es, kTileCh,
+  ok = ok && make_map(&d->tm_dout, p->dout, g.bf16, g.Dm, g.L, g.B, g.os * es, (uint64_t)g.L * g.os * es, kBTile,
                       kChunk);
   if (p->z)
-    ok = ok && make_map(&d->tm_z, p->z, g.bf16, g.Dm, g.L, g.B, g.zs * es, (uint64_t)g.L * g.zs * es, kTileCh,
+    ok = ok && make_map(&d->tm_z, p->z, g.bf16, g.Dm, g.L, g.B, g.zs * es, (uint64_t)g.L * g.zs * es, kBTile,
                         kChunk);
   else
     std::memset(&d->tm_z, 0, sizeof(d->tm_z));
-  ok = ok && make_map(&d->tm_states, p->states, false, kN, g.Dm, (uint64_t)g.B * g.nblk, kN * 4,
-                      (uint64_t)g.Dm * kN * 4, kN, kTileCh);
   if (!ok) return SSM_ERR_LAUNCH;  // detail recorded by make_map
+  d->states = p->states;
   d->A = p->A;
   d->D = p->D;
   d->bias = p->delta_bias;
@@ -375,7 +381,7 @@ static int fill_bwd_dir(const ssm_params_t* p, const Geo& g, const BwdWs& w, Bwd
   d->flags = p->flags;
   d->gate_act = p->z ? p->gate_act : SSM_ACT_NONE;
   d->has_z = p->z != nullptr;
-  const Seg sg = choose_segments(g, kBwdChainTarget);
+  const Seg sg = choose_segments(g, kBwdSeg);
   d->nseg = sg.nseg;
   d->seg_chunks = sg.seg_chunks;
   d->segF = w.segF;
@@ -393,15 +399,19 @@ static int launch_bwd_t(BwdLaunch& L, int ndir, const Geo& g, cudaStream_t s) {
     bytes = lay.bytes > bytes ? lay.bytes : bytes;
   }
   const int nseg = L.dir[0].nseg;
-  dim3 grid((g.Dm + kTileCh - 1) / kTileCh, g.B, 1);
+  dim3 grid((g.Dm + kBTile - 1) / kBTile, g.B, 1);
   if (nseg > 1) {  // segment pre-pass: adjoint carried out of every segment but the first
-    using SA = BwdAggSmem<T, TBC>;
+    int abytes = 0;
+    for (int d = 0; d < ndir; ++d) {
+      const BwdAggLayout al(sizeof(T), sizeof(TBC), L.dir[d].has_z != 0);
+      abytes = al.bytes > abytes ? al.bytes : abytes;
+    }
     auto agg = ssm_bwd_agg_kernel<T, TBC>;
-    SSM_CUDA_CHECK(cudaFuncSetAttribute(agg, cudaFuncAttributeMaxDynamicSharedMemorySize, SA::kBytes),
+    SSM_CUDA_CHECK(cudaFuncSetAttribute(agg, cudaFuncAttributeMaxDynamicSharedMemorySize, abytes),
                    "cudaFuncSetAttribute(ssm_bwd_agg_kernel)");
     L.zdiv = nseg - 1;
     grid.z = ndir * (nseg - 1);
-    agg<<<grid, kThreads, SA::kBytes, s>>>(L);
+    agg<<<grid, kBThreads, abytes, s>>>(L);
     SSM_CUDA_CHECK(cudaGetLastError(), "launch ssm_bwd_agg_kernel");
     dim3 fgrid((g.Dm * kN + 255) / 256, ndir, g.B);
     ssm_bwd_fold_kernel<<<fgrid, 256, 0, s>>>(L);
@@ -412,7 +422,7 @@ static int launch_bwd_t(BwdLaunch& L, int ndir, const Geo& g, cudaStream_t s) {
                  "cudaFuncSetAttribute(ssm_bwd_kernel)");
   L.zdiv = nseg;
   grid.z = ndir * nseg;
-  kern<<<grid, kThreads, bytes, s>>>(L);
+  kern<<<grid, kBThreads, bytes, s>>>(L);
   SSM_CUDA_CHECK(cudaGetLastError(), "launch ssm_bwd_kernel");
   return SSM_OK;
 }
@@ -449,7 +459,7 @@ static int launch_finalize(const ssm_params_t* p, const Geo& g, const BwdWs& w, 
   f.dB = p->dB;
   f.dC = p->dC;
   f.bc_stride = g.bs;
-  f.prows = g.B * choose_segments(g, kBwdChainTarget).nseg;
+  f.prows = g.B * choose_segments(g, kBwdSeg).nseg;
   f.batch = g.B;
   f.L = g.L;
   f.Dm = g.Dm;
@@ -479,7 +489,7 @@ extern "C" {
 
 size_t ssm_states_elems(const ssm_params_t* p) {
   if (!p || p->batch <= 0 || p->seqlen <= 0 || p->dim <= 0) return 0;
-  return (size_t)p->batch * ((p->seqlen + kChunk - 1) / kChunk) * p->dim * kN;
+  return (size_t)p->batch * ((p->seqlen + kCk - 1) / kCk) * p->dim * kN;
 }
 
 size_t ssm_workspace_bytes(const ssm_params_t* p) {
