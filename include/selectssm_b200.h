@@ -187,6 +187,9 @@ SSM_API int ssm_bwd_noalloc(const ssm_params_t* p, ssm_stream_t stream);
 /* Detail (CUDA error string and call site) of the most recent SSM_ERR_LAUNCH
  * returned on the calling host thread; "" if none. */
 SSM_API const char* ssm_last_error(void);
+/* Number of CUDA kernels this library has launched in this process (all
+ * devices, all host threads); a diagnostic for counting launches per call. */
+SSM_API unsigned long long ssm_launch_count(void);
 /* Library version string. */
 SSM_API const char* ssm_version(void);
 

@@ -41,7 +41,7 @@ DSTATE = 16
 EXPORTED_SYMBOLS = (
     "ssm_workspace_bytes", "ssm_states_elems", "ssm_fwd", "ssm_bwd", "ssm_fwd_bidir", "ssm_bwd_bidir",
     "ssm_conv1d_workspace_bytes", "ssm_conv1d_act_fwd", "ssm_conv1d_act_bwd", "ssm_strerror", "ssm_last_error",
-    "ssm_version", "ssm_bwd_noalloc",
+    "ssm_version", "ssm_bwd_noalloc", "ssm_launch_count",
 )
 
 
@@ -113,6 +113,7 @@ def load(path: str | None = None) -> ctypes.CDLL:
         "ssm_strerror": (ctypes.c_char_p, [ctypes.c_int]),
         "ssm_last_error": (ctypes.c_char_p, []),
         "ssm_version": (ctypes.c_char_p, []),
+        "ssm_launch_count": (ctypes.c_ulonglong, []),
         "ssm_bwd_noalloc": (ctypes.c_int, [P, ctypes.c_void_p]),
     }
     for name, (res, args) in sigs.items():

@@ -11,6 +11,9 @@
 
 namespace ssm {
 
+// Adds n to the library's count of kernels launched (ssm_launch_count).
+void note_launches(unsigned n);
+
 constexpr int kChunk = 16;        // steps per TMA stage
 constexpr int kCk = 8;            // forward checkpoint spacing (backward register block)
 constexpr int kN = 16;            // state size supported by this build

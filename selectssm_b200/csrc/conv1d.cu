@@ -216,6 +216,7 @@ int ssm_conv1d_act_fwd(const ssm_conv_params_t* p, ssm_stream_t stream) {
     conv_fwd_kernel<__nv_bfloat16><<<grid, block, 0, s>>>(a);
   else
     conv_fwd_kernel<float><<<grid, block, 0, s>>>(a);
+  note_launches(1);
   const cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? SSM_OK : launch_error("launch conv_fwd_kernel", e);
 }
@@ -245,6 +246,7 @@ int ssm_conv1d_act_bwd(const ssm_conv_params_t* p, ssm_stream_t stream) {
     conv_bwd_kernel<float><<<grid, block, 0, s>>>(a);
   const int n = a.K * a.Dm;
   conv_dw_reduce_kernel<<<(n + 255) / 256, 256, 0, s>>>(a.dw_part, p->dw, p->batch * a.nsegblk, a.K, a.Dm);
+  note_launches(2);
   const cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? SSM_OK : launch_error("launch conv_bwd_kernel", e);
 }

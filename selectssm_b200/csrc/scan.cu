@@ -2,6 +2,7 @@
 // their argument checks, TMA descriptor set-up and launch sequences.
 #include <cstdio>
 #include <cstring>
+#include <atomic>
 #include <mutex>
 
 #include "scan_bwd.cuh"
@@ -10,6 +11,9 @@ namespace ssm {
 
 // Detail of the most recent SSM_ERR_LAUNCH on this host thread (diagnostics only).
 thread_local char g_last_error[256] = "";
+std::atomic<unsigned long long> g_launches{0};
+
+void note_launches(unsigned n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
 
 int launch_error(const char* where, cudaError_t e) {
   snprintf(g_last_error, sizeof(g_last_error), "%s: %s", where, cudaGetErrorString(e));
@@ -293,7 +297,8 @@ static int launch_fwd_t(FwdLaunch& L, int ndir, const Geo& g, cudaStream_t s) {
     L.zdiv = nseg - 1;
     grid.z = ndir * (nseg - 1);
     agg<<<grid, kThreads, S::kBytes, s>>>(L);
-    SSM_CUDA_CHECK(cudaGetLastError(), "launch ssm_fwd_kernel<agg>");
+    note_launches(1);
+  SSM_CUDA_CHECK(cudaGetLastError(), "launch ssm_fwd_kernel<agg>");
   }
   auto kern = ssm_fwd_kernel<T, TBC, false>;
   SSM_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kBytes),
@@ -301,6 +306,7 @@ static int launch_fwd_t(FwdLaunch& L, int ndir, const Geo& g, cudaStream_t s) {
   L.zdiv = nseg;
   grid.z = ndir * nseg;
   kern<<<grid, kThreads, S::kBytes, s>>>(L);
+  note_launches(1);
   SSM_CUDA_CHECK(cudaGetLastError(), "launch ssm_fwd_kernel");
   return SSM_OK;
 }
@@ -412,10 +418,12 @@ static int launch_bwd_t(BwdLaunch& L, int ndir, const Geo& g, cudaStream_t s) {
     L.zdiv = nseg - 1;
     grid.z = ndir * (nseg - 1);
     agg<<<grid, kBThreads, abytes, s>>>(L);
-    SSM_CUDA_CHECK(cudaGetLastError(), "launch ssm_bwd_agg_kernel");
+    note_launches(1);
+  SSM_CUDA_CHECK(cudaGetLastError(), "launch ssm_bwd_agg_kernel");
     dim3 fgrid((g.Dm * kN + 255) / 256, ndir, g.B);
     ssm_bwd_fold_kernel<<<fgrid, 256, 0, s>>>(L);
-    SSM_CUDA_CHECK(cudaGetLastError(), "launch ssm_bwd_fold_kernel");
+    note_launches(1);
+  SSM_CUDA_CHECK(cudaGetLastError(), "launch ssm_bwd_fold_kernel");
   }
   auto kern = ssm_bwd_kernel<T, TBC>;
   SSM_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes),
@@ -423,6 +431,7 @@ static int launch_bwd_t(BwdLaunch& L, int ndir, const Geo& g, cudaStream_t s) {
   L.zdiv = nseg;
   grid.z = ndir * nseg;
   kern<<<grid, kBThreads, bytes, s>>>(L);
+  note_launches(1);
   SSM_CUDA_CHECK(cudaGetLastError(), "launch ssm_bwd_kernel");
   return SSM_OK;
 }
@@ -442,6 +451,7 @@ static int launch_zero_acc(const Geo& g, const BwdWs& w, cudaStream_t s) {
   const unsigned blocks = (unsigned)((n + threads - 1) / threads);
   zero_rows16_kernel<<<blocks, threads, 0, s>>>(w.dB_acc, rows, w.acc_stride);
   zero_rows16_kernel<<<blocks, threads, 0, s>>>(w.dC_acc, rows, w.acc_stride);
+  note_launches(2);
   SSM_CUDA_CHECK(cudaGetLastError(), "launch zero_rows16_kernel");
   return SSM_OK;
 }
@@ -473,6 +483,7 @@ static int launch_finalize(const ssm_params_t* p, const Geo& g, const BwdWs& w, 
     finalize_kernel<__nv_bfloat16><<<blocks, threads, 0, s>>>(f);
   else
     finalize_kernel<float><<<blocks, threads, 0, s>>>(f);
+  note_launches(1);
   SSM_CUDA_CHECK(cudaGetLastError(), "launch finalize_kernel");
   return SSM_OK;
 }
@@ -589,6 +600,8 @@ const char* ssm_strerror(int status) {
     default: return "unknown status";
   }
 }
+
+unsigned long long ssm_launch_count(void) { return ssm::g_launches.load(std::memory_order_relaxed); }
 
 const char* ssm_version(void) { return "selectssm_b200 0.1.0 (sm_100a)"; }
 
