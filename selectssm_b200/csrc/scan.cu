@@ -6,6 +6,7 @@
 #include <mutex>
 
 #include "scan_bwd.cuh"
+#include "scan_fwd.cuh"
 
 namespace ssm {
 
@@ -193,38 +194,56 @@ static int check_bwd(const ssm_params_t* p, Geo* g) {
 
 static size_t round256(size_t x) { return (x + 255) & ~size_t(255); }
 
-// Sequence segments.  A (batch row, 32-channel tile) pair is one chain of
-// ceil(L/16) dependent chunks; when there are too few such chains to fill the
-// GPU (measured: about 384 concurrent chains, 2.6 per SM on 148 SMs, saturate
-// it), the sequence is cut into segments that run concurrently, at the cost of
-// one extra recurrence pass for the carries.  The choice depends on the shape
-// only, so results do not depend on the device.
+// Sequence segments.  A (batch row, channel tile) is one chain of steps; with
+// few chains the sequence is cut into segments that run as separate CTAs, at
+// the price of a pre-pass over all segments but the last (it produces each
+// segment's end state / carry) and a fold.  The segment count minimises a
+// model of the run time in units of "one CTA processing one 16-step stage":
+//   waves(main) x stages per segment + r x waves(pre-pass) x stages per segment
+//   + a small per-segment cost,
+// where waves = ceil(CTAs / resident CTAs on the GPU).  Whole waves matter
+// because every CTA of a wave runs at about the same speed, so a last wave
+// that is a quarter full costs as much as a full one.  The resident counts are
+// the kernels' occupancy on a 148-SM B200 and are fixed here (not queried), so
+// workspace sizes stay a function of the shapes alone.
 struct Seg {
   int nseg, seg_chunks;
 };
-// The forward pre-pass repeats most of the forward's work, so the forward only
-// segments to reach ~384 chains; the backward pre-pass is a light adjoint-only
-// sweep, so the backward segments further, to ~2 waves of 4 CTAs per SM.
-// Targets count CTAs: the forward's 32-channel CTAs and the backward's
-// 128-channel CTAs (2 resident per SM: aim at 2 waves).
 struct SegPolicy {
-  long target;
-  int tile;
+  int tile;         // channels per CTA
+  long slots;       // resident CTAs of the main kernel on the GPU
+  long agg_slots;   // resident CTAs of the pre-pass
+  double agg_cost;  // pre-pass cost of one stage relative to the main kernel's
 };
-constexpr SegPolicy kFwdSeg{384, kTileCh};
-constexpr SegPolicy kBwdSeg{2L * 2 * 148, kBTile};
+constexpr int kSMs = 148;
+// The forward's 64-thread CTAs are latency bound and share an SM well (up to 7
+// resident), so a "wave" is taken as the measured sweet spot of 1536 CTAs.
+constexpr SegPolicy kFwdSeg{kTileCh, 1536, 1536, 0.55};
+constexpr SegPolicy kBwdSeg{kBTile, 2L * kSMs, 4L * kSMs, 0.5};
 
 static Seg choose_segments(const Geo& g, SegPolicy pol) {
-  const long target = pol.target;
   const int nblk = (g.L + kChunk - 1) / kChunk;
   if (nblk == 0) return {1, 1};
   const long chains = (long)((g.Dm + pol.tile - 1) / pol.tile) * g.B;
-  int nseg = chains > 0 ? (int)((target + chains - 1) / chains) : 1;
-  const int max_seg = nblk / 4;  // at least 4 chunks (64 steps) per segment
-  if (nseg > max_seg) nseg = max_seg;
-  if (nseg < 1) nseg = 1;
-  const int seg_chunks = (nblk + nseg - 1) / nseg;
-  return {(nblk + seg_chunks - 1) / seg_chunks, seg_chunks};
+  if (chains <= 0) return {1, nblk};
+  int max_seg = nblk / 4;  // at least 4 stages (64 steps) per segment
+  if (max_seg < 1) max_seg = 1;
+  if (max_seg > 64) max_seg = 64;
+  double best = 0.0;
+  Seg pick{1, nblk};
+  for (int n = 1; n <= max_seg; ++n) {
+    const int seg_chunks = (nblk + n - 1) / n;
+    const int nseg = (nblk + seg_chunks - 1) / seg_chunks;
+    if (nseg != n) continue;  // the same split as a smaller n
+    const long waves = (chains * nseg + pol.slots - 1) / pol.slots;
+    const long agg_waves = (chains * (nseg - 1) + pol.agg_slots - 1) / pol.agg_slots;
+    const double cost = (double)waves * seg_chunks + pol.agg_cost * (double)agg_waves * seg_chunks + 0.25 * nseg;
+    if (n == 1 || cost < best) {
+      best = cost;
+      pick = {nseg, seg_chunks};
+    }
+  }
+  return pick;
 }
 
 static size_t fwd_ws_bytes(const Geo& g) {
@@ -287,25 +306,25 @@ static int fill_fwd_dir(const ssm_params_t* p, const Geo& g, FwdDir* d) {
 
 template <typename T, typename TBC>
 static int launch_fwd_t(FwdLaunch& L, int ndir, const Geo& g, cudaStream_t s) {
-  using S = FwdSmem<T, TBC>;
+  using S = FwdSmem2<T, TBC>;
   const int nseg = L.dir[0].nseg;
   dim3 grid((g.Dm + kTileCh - 1) / kTileCh, g.B, 1);
   if (nseg > 1) {  // segment pre-pass: end state of every segment but the last
-    auto agg = ssm_fwd_kernel<T, TBC, true>;
+    auto agg = ssm_fwd2_kernel<T, TBC, true, kFEmu>;
     SSM_CUDA_CHECK(cudaFuncSetAttribute(agg, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kBytes),
                    "cudaFuncSetAttribute(ssm_fwd_kernel<agg>)");
     L.zdiv = nseg - 1;
     grid.z = ndir * (nseg - 1);
-    agg<<<grid, kThreads, S::kBytes, s>>>(L);
+    agg<<<grid, kFThreads, S::kBytes, s>>>(L);
     note_launches(1);
   SSM_CUDA_CHECK(cudaGetLastError(), "launch ssm_fwd_kernel<agg>");
   }
-  auto kern = ssm_fwd_kernel<T, TBC, false>;
+  auto kern = ssm_fwd2_kernel<T, TBC, false, kFEmu>;
   SSM_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kBytes),
                  "cudaFuncSetAttribute(ssm_fwd_kernel)");
   L.zdiv = nseg;
   grid.z = ndir * nseg;
-  kern<<<grid, kThreads, S::kBytes, s>>>(L);
+  kern<<<grid, kFThreads, S::kBytes, s>>>(L);
   note_launches(1);
   SSM_CUDA_CHECK(cudaGetLastError(), "launch ssm_fwd_kernel");
   return SSM_OK;
@@ -395,7 +414,7 @@ static int fill_bwd_dir(const ssm_params_t* p, const Geo& g, const BwdWs& w, Bwd
   return SSM_OK;
 }
 
-template <typename T, typename TBC>
+template <typename T, typename TBC, int G>
 static int launch_bwd_t(BwdLaunch& L, int ndir, const Geo& g, cudaStream_t s) {
   int bytes = 0;
   for (int d = 0; d < ndir; ++d) {
@@ -412,7 +431,7 @@ static int launch_bwd_t(BwdLaunch& L, int ndir, const Geo& g, cudaStream_t s) {
       const BwdAggLayout al(sizeof(T), sizeof(TBC), L.dir[d].has_z != 0);
       abytes = al.bytes > abytes ? al.bytes : abytes;
     }
-    auto agg = ssm_bwd_agg_kernel<T, TBC>;
+    auto agg = ssm_bwd_agg_kernel<T, TBC, G>;
     SSM_CUDA_CHECK(cudaFuncSetAttribute(agg, cudaFuncAttributeMaxDynamicSharedMemorySize, abytes),
                    "cudaFuncSetAttribute(ssm_bwd_agg_kernel)");
     L.zdiv = nseg - 1;
@@ -425,7 +444,7 @@ static int launch_bwd_t(BwdLaunch& L, int ndir, const Geo& g, cudaStream_t s) {
     note_launches(1);
   SSM_CUDA_CHECK(cudaGetLastError(), "launch ssm_bwd_fold_kernel");
   }
-  auto kern = ssm_bwd_kernel<T, TBC>;
+  auto kern = ssm_bwd_kernel<T, TBC, G>;
   SSM_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes),
                  "cudaFuncSetAttribute(ssm_bwd_kernel)");
   L.zdiv = nseg;
@@ -436,11 +455,27 @@ static int launch_bwd_t(BwdLaunch& L, int ndir, const Geo& g, cudaStream_t s) {
   return SSM_OK;
 }
 
+template <typename T, typename TBC>
+static int launch_bwd_g(BwdLaunch& L, int ndir, const Geo& g, cudaStream_t s) {
+  switch (L.dir[0].gate_act) {
+    case SSM_ACT_SILU: return launch_bwd_t<T, TBC, SSM_ACT_SILU>(L, ndir, g, s);
+    case SSM_ACT_GELU: return launch_bwd_t<T, TBC, SSM_ACT_GELU>(L, ndir, g, s);
+    case SSM_ACT_RELU: return launch_bwd_t<T, TBC, SSM_ACT_RELU>(L, ndir, g, s);
+    default: return launch_bwd_t<T, TBC, SSM_ACT_NONE>(L, ndir, g, s);
+  }
+}
+
 static int launch_bwd(BwdLaunch& L, int ndir, const Geo& g, cudaStream_t s) {
-  if (!g.bf16 && !g.bcbf16) return launch_bwd_t<float, float>(L, ndir, g, s);
-  if (!g.bf16 && g.bcbf16) return launch_bwd_t<float, __nv_bfloat16>(L, ndir, g, s);
-  if (g.bf16 && !g.bcbf16) return launch_bwd_t<__nv_bfloat16, float>(L, ndir, g, s);
-  return launch_bwd_t<__nv_bfloat16, __nv_bfloat16>(L, ndir, g, s);
+  if (ndir == 2 && L.dir[0].gate_act != L.dir[1].gate_act) {  // one launch per gate
+    BwdLaunch L1 = L;
+    L1.dir[0] = L.dir[1];
+    const int st = launch_bwd(L, 1, g, s);
+    return st ? st : launch_bwd(L1, 1, g, s);
+  }
+  if (!g.bf16 && !g.bcbf16) return launch_bwd_g<float, float>(L, ndir, g, s);
+  if (!g.bf16 && g.bcbf16) return launch_bwd_g<float, __nv_bfloat16>(L, ndir, g, s);
+  if (g.bf16 && !g.bcbf16) return launch_bwd_g<__nv_bfloat16, float>(L, ndir, g, s);
+  return launch_bwd_g<__nv_bfloat16, __nv_bfloat16>(L, ndir, g, s);
 }
 
 static int launch_zero_acc(const Geo& g, const BwdWs& w, cudaStream_t s) {

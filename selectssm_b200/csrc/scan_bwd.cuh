@@ -127,7 +127,9 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
       : "memory");
 }
 
-template <typename T, typename TBC>
+// G: the gate activation (an ssm_act code), fixed per launch so the step loops
+// hold no branch on it.
+template <typename T, typename TBC, int G>
 __global__ void __launch_bounds__(kBThreads, 2) ssm_bwd_kernel(const __grid_constant__ BwdLaunch P) {
   const BwdDir& a = P.dir[blockIdx.z / P.zdiv];
   const int seg = blockIdx.z % P.zdiv;
@@ -262,7 +264,7 @@ __global__ void __launch_bounds__(kBThreads, 2) ssm_bwd_kernel(const __grid_cons
         dxv[u] = valid ? dt * x : 0.f;
         const int row = rev ? kChunk - 1 - tl : tl;
         float g = ld_f(sdo + row * kBTile);
-        if (has_z) g *= act_f(ld_f(szo + row * kBTile), a.gate_act);
+        if (has_z) g *= act_f(ld_f(szo + row * kBTile), G);
         dyv[u] = valid ? g : 0.f;
       }
       // ---- restart state (the forward's checkpoint before this block)
@@ -306,7 +308,7 @@ __global__ void __launch_bounds__(kBThreads, 2) ssm_bwd_kernel(const __grid_cons
           const int l = rev ? L - 1 - t : t;
           float pre = y2.x + y2.y;
           if (has_D) pre = fmaf(Dso, mirror ? ld_f(suo + row * kBTile) : ld_f(su + tl * kBTile), pre);
-          const float g = ld_f(sdo + row * kBTile) * pre * act_grad_f(ld_f(szo + row * kBTile), a.gate_act);
+          const float g = ld_f(sdo + row * kBTile) * pre * act_grad_f(ld_f(szo + row * kBTile), G);
           st_act(dz_g + (size_t)l * a.z_stride, g);
         }
       }
@@ -350,7 +352,7 @@ __global__ void __launch_bounds__(kBThreads, 2) ssm_bwd_kernel(const __grid_cons
             float sg = dyv[u];
             if (mirror) {
               sg = ld_f(sds + tl * kBTile);
-              if (has_z) sg *= act_f(ld_f(szs + tl * kBTile), a.gate_act);
+              if (has_z) sg *= act_f(ld_f(szs + tl * kBTile), G);
             }
             du = fmaf(Dsc, sg, du);
             dD_acc = fmaf(sg, x, dD_acc);
@@ -426,7 +428,7 @@ struct BwdAggLayout {
   }
 };
 
-template <typename T, typename TBC>
+template <typename T, typename TBC, int G>
 __global__ void __launch_bounds__(kBThreads, 4) ssm_bwd_agg_kernel(const __grid_constant__ BwdLaunch P) {
   const BwdDir& a = P.dir[blockIdx.z / P.zdiv];
   const int seg = 1 + blockIdx.z % P.zdiv;  // segments 1 .. nseg-1
@@ -505,7 +507,7 @@ __global__ void __launch_bounds__(kBThreads, 4) ssm_bwd_agg_kernel(const __grid_
       tsum += dt;
       const int row = rev ? kChunk - 1 - tl : tl;
       float g = ld_f(sdo + row * kBTile);
-      if (has_z) g *= act_f(ld_f(szo + row * kBTile), a.gate_act);
+      if (has_z) g *= act_f(ld_f(szo + row * kBTile), G);
       const float2 dy2 = dup2(valid ? g : 0.f), dt2 = dup2(dt);
       float2 Cq[8];
       ld16q(sC + tl * kN, 0, Cq);
