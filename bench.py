@@ -173,18 +173,21 @@ def cpu_threads():
         return 1
 
 
-def run_cpu_sample(seqlen=256, reps=1):
+def run_cpu_sample(seqlen=4096, reps=1, warm_seqlen=256):
+    """Oracle fwd+bwd on one batch row of the workload (the full sequence by
+    default: about 5-15 s of CPU work), after a short warm-up."""
     B, D, N = 1, CFG["dim"], CFG["dstate"]
+    cpu_reference_step(host_inputs(1, B, warm_seqlen, D, N))  # warm
     inp = host_inputs(0, B, seqlen, D, N)
-    cpu_reference_step(inp)  # warm
     t0 = time.perf_counter()
     for _ in range(reps):
         cpu_reference_step(inp)
     dt = (time.perf_counter() - t0) / reps
     units = B * seqlen * D
     sample = (f"NumPy restatement of the reference algorithm (chunked scan fwd + custom-VJP bwd, "
-              f"float32) on a prefix batch=1, L={seqlen}, d_inner={D}, N={N} of the config-2 workload; "
-              f"{reps} rep(s) after 1 warm-up; elementwise work single-threaded, BLAS threads {cpu_threads()}")
+              f"float32) on one batch row of the config-2 workload: batch=1, L={seqlen}, d_inner={D}, N={N}; "
+              f"{reps} rep(s) after a warm-up at L={warm_seqlen}; elementwise work single-threaded, "
+              f"BLAS threads {cpu_threads()}")
     return units / dt, dt, sample
 
 
@@ -196,7 +199,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--e2e-steps", type=int, default=8)
     ap.add_argument("--batch", type=int, default=None, help="override batch per GPU (small profiling cases)")
     args = ap.parse_args()
 
@@ -217,10 +220,10 @@ def main():
         steps = max(1, args.steps)
         vals = []
         for _ in range(args.warmup):
-            run_cpu_sample(seqlen=64)
+            run_cpu_sample(seqlen=64, warm_seqlen=64)
         t0 = time.perf_counter()
         for _ in range(steps):
-            v, _, sample = run_cpu_sample(seqlen=128)
+            v, _, sample = run_cpu_sample(seqlen=128, warm_seqlen=16)
             vals.append(v)
         total = time.perf_counter() - t0
         v = statistics.median(vals)
@@ -288,9 +291,13 @@ def main():
     units = Bsz * L * D
     value = units * world / (ms * 1e-3)
 
-    # --- per-kernel timing of the forward and backward calls (same stream)
+    # --- per-call timing of the forward and backward (same stream).  The calls
+    # are queued back to back, as in the training loop, so host-side overhead
+    # overlaps the GPU work and the events time the kernels.
     p_fwd, p_bwd = [], []
-    for _ in range(5):
+    marks = []
+    torch.cuda.synchronize()
+    for _ in range(8):
         a0, a1, a2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
         for k in ("u", "delta", "z", "A", "B", "C", "D"):
             t[k].grad = None
@@ -299,7 +306,9 @@ def main():
         a1.record(stream)
         out.backward(t["dout"])
         a2.record(stream)
-        torch.cuda.synchronize()
+        marks.append((a0, a1, a2))
+    torch.cuda.synchronize()
+    for a0, a1, a2 in marks[1:]:
         p_fwd.append(a0.elapsed_time(a1))
         p_bwd.append(a1.elapsed_time(a2))
     t_fwd, t_bwd = statistics.median(p_fwd), statistics.median(p_bwd)
@@ -311,7 +320,7 @@ def main():
                 "ms": t_bwd}
     roof_bwd["frac"] = roof_bwd["achieved"] / hbm
     roof_fwd = {"kernel": "ssm_fwd call: ssm_fwd_kernel<float,float> + segment pre-pass", "bound": "hbm", "achieved": fb / (t_fwd * 1e-3) / 1e9,
-                "peak": hbm, "unit": "GB/s", "traffic": read_traffic("ssm_fwd_kernel_config2.md"),
+                "peak": hbm, "unit": "GB/s", "traffic": read_traffic("ssm_fwd2_kernel_config2.md"),
                 "algorithmic_bytes": fb, "ms": t_fwd}
     roof_fwd["frac"] = roof_fwd["achieved"] / hbm
     step_roof = {"achieved": (fb + bb) / (ms * 1e-3) / 1e9, "peak": hbm, "unit": "GB/s"}
@@ -319,30 +328,57 @@ def main():
 
     # --- end to end through the public API: pinned host inputs -> device, fwd+bwd,
     # outputs and gradients -> pinned host
+    # Pipelined over steps on three streams: the upload of step i+1 (copy_in)
+    # and the download of step i-1 (copy_out) overlap the compute of step i;
+    # every step still moves all of its inputs and results across PCIe.
     pin = {k: torch.from_numpy(v).pin_memory() for k, v in h.items()}
     h2d = sum(v.numel() * v.element_size() for v in pin.values())
-    outs_host = []
+    grad_keys = ("u", "delta", "z", "A", "B", "C", "D")
+    slots = [{k: torch.empty(v.shape, dtype=v.dtype, device=dev).requires_grad_(k in grad_keys)
+              for k, v in pin.items()} for _ in range(2)]
+    copy_in, copy_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    ev_in = [torch.cuda.Event() for _ in range(2)]
+    ev_done = [torch.cuda.Event() for _ in range(2)]
+    outs_host = [None, None]
 
-    def e2e_step():
-        dv = {k: v.to(dev, non_blocking=True) for k, v in pin.items()}
-        for k in ("u", "delta", "z", "A", "B", "C", "D"):
-            dv[k].requires_grad_(True)
-        out = step(dv)
-        res = [out.detach()] + [dv[k].grad for k in ("u", "delta", "z", "A", "B", "C", "D")]
-        if not outs_host:  # pinned result buffers, allocated once before the timed region
-            outs_host.extend(torch.empty(r.shape, dtype=r.dtype, pin_memory=True) for r in res)
-        for hbuf, r in zip(outs_host, res):
-            hbuf.copy_(r, non_blocking=True)
+    def upload(s):
+        copy_in.wait_event(ev_done[s])  # the slot's previous step has finished reading it
+        with torch.cuda.stream(copy_in), torch.no_grad():
+            for k, v in pin.items():
+                slots[s][k].copy_(v, non_blocking=True)
+        ev_in[s].record(copy_in)
 
-    e2e_step()
-    d2h = sum(r.numel() * r.element_size() for r in outs_host)
+    def run(i):
+        s = i % 2
+        stream.wait_event(ev_in[s])
+        out = step(slots[s])
+        res = [out.detach()] + [slots[s][k].grad for k in grad_keys]
+        ev_done[s].record(stream)
+        if outs_host[s] is None:  # pinned result buffers, allocated before the timed region
+            outs_host[s] = [torch.empty(r.shape, dtype=r.dtype, pin_memory=True) for r in res]
+        copy_out.wait_event(ev_done[s])
+        with torch.cuda.stream(copy_out):
+            for hb, r in zip(outs_host[s], res):
+                hb.copy_(r, non_blocking=True)
+                r.record_stream(copy_out)
+
+    def pipeline(n):
+        upload(0)
+        for i in range(n):
+            if i + 1 < n:
+                upload((i + 1) % 2)
+            run(i)
+        stream.wait_stream(copy_out)
+
+    pipeline(2)
+    torch.cuda.synchronize()
+    d2h = sum(r.numel() * r.element_size() for r in outs_host[0])
     ee0, ee1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
     ee0.record(stream)
-    for _ in range(args.e2e_steps):
-        e2e_step()
+    pipeline(args.e2e_steps)
     ee1.record(stream)
     torch.cuda.synchronize()
     ems = ee0.elapsed_time(ee1) / args.e2e_steps
@@ -360,7 +396,7 @@ def main():
             "gpu_launches": n_launches,
             "clocks": clk.summary(), "library": lib.ssm_version().decode()}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        v, secs, sample = run_cpu_sample(seqlen=256)
+        v, secs, sample = run_cpu_sample()
         line["cpu_baseline"] = {"value": v, "unit": UNIT, "cores": cpu_threads(), "kind": "port",
                                 "sample": sample, "seconds": secs}
     if rank == 0:

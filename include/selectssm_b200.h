@@ -4,8 +4,8 @@
  * The reference (ihh/selectssm) is JAX/Flax.  Its hot path is a set of Python
  * functions traced under jit; the FFI a JAX maintainer would bind for it is an
  * XLA custom call (jax.ffi) per function.  Each entry point below is the plain
- * C function such a custom-call handler wraps (see INTEGRATION.md for the
- * handler shim and for the ctypes binding the tests use):
+ * C function such a custom-call handler wraps; the tests and the Python host
+ * bind the same functions with ctypes:
  *
  *   ssm_fwd        replaces ssm_chunked_scan / ssm_recursive_scan / ssm_scan
  *                  forward (src/selectssm/selectssm.py:37-109,
@@ -121,7 +121,9 @@ typedef struct ssm_params {
                                            failure (bounded wait gave up)                 */
 } ssm_params_t;
 
-/* Bytes of scratch the backward needs for these params (the forward needs none). */
+/* Bytes of scratch (p->workspace) that ssm_fwd and ssm_bwd need for these
+ * params: the forward uses it when it splits the sequence into segments, the
+ * backward always; one buffer of this size serves both calls. */
 SSM_API size_t ssm_workspace_bytes(const ssm_params_t* p);
 /* Number of floats of p->states: B * ceil(L/8) * D * N. */
 SSM_API size_t ssm_states_elems(const ssm_params_t* p);
@@ -137,8 +139,9 @@ SSM_API int ssm_bwd(const ssm_params_t* p, ssm_stream_t stream);
  * SSM_COMPLEMENT when complement=True); they may share z (tie_gate) and write
  * disjoint channel ranges of one output (concatenate_fwd_rev).  When z is shared,
  * dz must not be: the two directions' dz are separate buffers for the caller to add.
- * Shapes and dtypes of the two sets must match; workspace must hold
- * ssm_workspace_bytes(fwd) + ssm_workspace_bytes(rev) in fwd->workspace.       */
+ * Shapes and dtypes of the two sets must match.  Scratch: ssm_fwd_bidir uses
+ * each set's own workspace; ssm_bwd_bidir uses fwd->workspace only, which must
+ * then hold ssm_workspace_bytes(fwd) + ssm_workspace_bytes(rev).               */
 SSM_API int ssm_fwd_bidir(const ssm_params_t* fwd, const ssm_params_t* rev, ssm_stream_t stream);
 SSM_API int ssm_bwd_bidir(const ssm_params_t* fwd, const ssm_params_t* rev, ssm_stream_t stream);
 

@@ -18,3 +18,4 @@ from .ops import (  # noqa: F401
 
 __version__ = "0.1.0"
 from .modules import BidirectionalMamba, SelectiveSSM  # noqa: F401,E402
+from .rcps import RCPSEmbedding, RCPSLMHead, RCPSNorm, RCPSWrapper, rc_conjugate  # noqa: F401,E402

@@ -252,7 +252,9 @@ __global__ void __launch_bounds__(kBThreads, 2) ssm_bwd_kernel(const __grid_cons
       const int T0 = blk * kCk;
       const int ck = j * (kChunk / kCk) + blk;  // global 8-step block index
       // ---- per-step scalars of the block (own channel)
-      float dtv[kCk], dxv[kCk], dyv[kCk];
+      // (sgv: upstream gradient of the skip term in the scan frame; it differs
+      // from dyv only for the reference's reverse-skip frame)
+      float dtv[kCk], dxv[kCk], dyv[kCk], sgv[kCk];
 #pragma unroll
       for (int u = 0; u < kCk; ++u) {
         const int tl = T0 + u;
@@ -266,6 +268,16 @@ __global__ void __launch_bounds__(kBThreads, 2) ssm_bwd_kernel(const __grid_cons
         float g = ld_f(sdo + row * kBTile);
         if (has_z) g *= act_f(ld_f(szo + row * kBTile), G);
         dyv[u] = valid ? g : 0.f;
+        sgv[u] = dyv[u];
+      }
+      if (mirror) {
+#pragma unroll
+        for (int u = 0; u < kCk; ++u) {
+          const int tl = T0 + u;
+          float sg = ld_f(sds + tl * kBTile);
+          if (has_z) sg *= act_f(ld_f(szs + tl * kBTile), G);
+          sgv[u] = j * kChunk + tl < L ? sg : 0.f;
+        }
       }
       // ---- restart state (the forward's checkpoint before this block)
       float2 h[8];
@@ -302,14 +314,14 @@ __global__ void __launch_bounds__(kBThreads, 2) ssm_bwd_kernel(const __grid_cons
         const float dc = reduce32ch(vc, b2, b1);
         if (red_writer) red[(warp * kChunk + tl) * 32 + kN + red_n] = dc;
         // dz needs the pre-gate output of this step
-        const int t = j * kChunk + tl;
-        if (has_z && t < L && cvalid) {
+        if (has_z) {  // straight-line; only the store is predicated
+          const int t = j * kChunk + tl;
           const int row = rev ? kChunk - 1 - tl : tl;
           const int l = rev ? L - 1 - t : t;
-          float pre = y2.x + y2.y;
-          if (has_D) pre = fmaf(Dso, mirror ? ld_f(suo + row * kBTile) : ld_f(su + tl * kBTile), pre);
+          const float xs = ld_f(mirror ? suo + row * kBTile : su + tl * kBTile);
+          const float pre = fmaf(Dso, xs, y2.x + y2.y);  // Dso is 0 without a skip
           const float g = ld_f(sdo + row * kBTile) * pre * act_grad_f(ld_f(szo + row * kBTile), G);
-          st_act(dz_g + (size_t)l * a.z_stride, g);
+          if (t < L && cvalid) st_act(dz_g + (size_t)l * a.z_stride, g);
         }
       }
       tmem_wait_st();
@@ -344,22 +356,17 @@ __global__ void __launch_bounds__(kBThreads, 2) ssm_bwd_kernel(const __grid_cons
         const float db = reduce32ch(vb, b2, b1);
         if (red_writer) red[(warp * kChunk + tl) * 32 + red_n] = db;
         // du, ddelta and the skip gradients of this step
+        // straight-line (steps past L and lanes past Dm hold zeros); only the
+        // stores are predicated
         const int t = j * kChunk + tl;
+        const float x = ld_f(su + tl * kBTile);
+        const float du = fmaf(Dsc, sgv[u], dtv[u] * sbf);  // Dsc is 0 without a skip
+        dD_acc = fmaf(sgv[u], x, dD_acc);
+        float g = fmaf(x, sbf, saw);  // d/d dt
+        const float sig = sigmoid_f(ld_f(sd + tl * kBTile) + bias);
+        g *= softplus ? sig : 1.f;
+        db_acc += g;
         if (t < L && cvalid) {
-          const float x = ld_f(su + tl * kBTile);
-          float du = dtv[u] * sbf;
-          if (has_D) {
-            float sg = dyv[u];
-            if (mirror) {
-              sg = ld_f(sds + tl * kBTile);
-              if (has_z) sg *= act_f(ld_f(szs + tl * kBTile), G);
-            }
-            du = fmaf(Dsc, sg, du);
-            dD_acc = fmaf(sg, x, dD_acc);
-          }
-          float g = fmaf(x, sbf, saw);  // d/d dt
-          if (softplus) g *= sigmoid_f(ld_f(sd + tl * kBTile) + bias);
-          db_acc += g;
           st_act(du_g + (size_t)t * Dm, du);
           st_act(dd_g + (size_t)t * Dm, g);
         }
@@ -413,6 +420,10 @@ __global__ void __launch_bounds__(kBThreads, 2) ssm_bwd_kernel(const __grid_cons
 // f_t = C_t dy_t + f_{t+1} alpha_{t+1} over the segment from a zero carry and
 // writes the carry leaving its first step (f alpha, natural state order) and
 // the segment's sum of dt.  Reads delta, C, dout and z only.
+// State pairs per lane whose exponential the pre-pass evaluates on the FMA
+// pipe (ex2_poly2): the pre-pass is otherwise bound by the MUFU unit.
+constexpr int kAggEmu = 1;
+
 struct BwdAggLayout {
   int offDelta, offDo, offZo, offC, stage, offBars, bytes;
   __host__ __device__ BwdAggLayout(int es, int esbc, bool has_z) {
@@ -514,7 +525,8 @@ __global__ void __launch_bounds__(kBThreads, 4) ssm_bwd_agg_kernel(const __grid_
 #pragma unroll
       for (int p = 0; p < 8; ++p) {
         const float2 e = fmul2(A2[p], dt2);
-        fa[p] = fmul2(ffma2(Cq[p], dy2, fa[p]), make_float2(ex2(e.x), ex2(e.y)));
+        const float2 al = p < kAggEmu ? ex2_poly2(e) : make_float2(ex2(e.x), ex2(e.y));
+        fa[p] = fmul2(ffma2(Cq[p], dy2, fa[p]), al);
       }
     }
     __syncthreads();

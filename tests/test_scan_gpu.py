@@ -171,6 +171,66 @@ def test_bidir_single_launch(cuda, complement):
     assert relerr(to_np(zt.grad), gf["dz"] + gr["dz"]) < 1e-4
 
 
+@pytest.mark.parametrize("act_dtype,bc_dtype,gate", [(torch.float32, torch.bfloat16, "none"),
+                                                      (torch.bfloat16, torch.float32, "silu"),
+                                                      (torch.float32, torch.float32, "none")])
+def test_mixed_bc_dtype_and_identity_gate(cuda, act_dtype, bc_dtype, gate):
+    """B / C in a different dtype than the activations, and the identity gate
+    (y * z); the oracle sees the same rounded inputs."""
+    import selectssm_b200 as S
+    Bsz, L, D = 2, 77, 48
+    inp = make(Bsz, L, D, 11, torch.float32)
+    for dt_, keys in ((act_dtype, ("u", "z", "delta", "dout")), (bc_dtype, ("B", "C"))):
+        if dt_ == torch.bfloat16:
+            for k in keys:
+                inp[k] = to_np(torch.from_numpy(inp[k]).to(torch.bfloat16))
+    kw = dict(D=inp["D"], z=inp["z"], delta_bias=inp["bias"], delta_softplus=True, gate_act=gate)
+    ref_out = O.selective_scan_fwd(inp["u"], inp["delta"], inp["A"], inp["B"], inp["C"], **kw)
+    ref = O.selective_scan_bwd(inp["u"], inp["delta"], inp["A"], inp["B"], inp["C"], inp["dout"], **kw)
+    ts = {k: to_t(inp[k], cuda, act_dtype).requires_grad_() for k in ("u", "delta", "z")}
+    ts.update({k: to_t(inp[k], cuda, bc_dtype).requires_grad_() for k in ("B", "C")})
+    ts.update({k: to_t(inp[k], cuda).requires_grad_() for k in ("A", "D", "bias")})
+    out = S.selective_scan(ts["u"], ts["delta"], ts["A"], ts["B"], ts["C"], D=ts["D"], z=ts["z"],
+                           delta_bias=ts["bias"], delta_softplus=True, gate_act=gate)
+    tol = 2e-2 if torch.bfloat16 in (act_dtype, bc_dtype) else 1e-4
+    assert relerr(to_np(out), ref_out) < tol
+    out.backward(to_t(inp["dout"], cuda, act_dtype))
+    for name, k in (("du", "u"), ("ddelta", "delta"), ("dz", "z"), ("dA", "A"), ("dB", "B"), ("dC", "C"),
+                    ("dD", "D"), ("ddelta_bias", "bias")):
+        assert ts[k].grad.dtype == ts[k].dtype
+        assert relerr(to_np(ts[k].grad), ref[name]) < tol, name
+
+
+def test_bidir_gate_on_one_direction(cuda):
+    """Forward direction gated by z, reverse direction ungated: the backward
+    runs one launch per gate and must still match the oracle."""
+    import selectssm_b200 as S
+    Bsz, L, D = 1, 90, 32
+    f = make(Bsz, L, D, 21, torch.float32)
+    r = make(Bsz, L, D, 22, torch.float32)
+
+    def leaves(d):
+        return [to_t(d[k], cuda).requires_grad_() for k in ("u", "delta", "A", "B", "C", "D", "bias")]
+
+    lf, lr = leaves(f), leaves(r)
+    zt = to_t(f["z"], cuda).requires_grad_()
+    out = S.selective_scan_bidir(*lf, zt, *lr, None, complement=True)
+    dout = np.random.default_rng(23).standard_normal((Bsz, L, 2 * D))
+    out.backward(to_t(dout, cuda))
+    kwf = dict(D=f["D"], z=f["z"], delta_bias=f["bias"], delta_softplus=True)
+    kwr = dict(D=r["D"], z=None, delta_bias=r["bias"], delta_softplus=True, reverse=True, complement=True)
+    assert relerr(to_np(out[..., :D]), O.selective_scan_fwd(f["u"], f["delta"], f["A"], f["B"], f["C"], **kwf)) < 1e-4
+    assert relerr(to_np(out[..., D:]), O.selective_scan_fwd(r["u"], r["delta"], r["A"], r["B"], r["C"], **kwr)) < 1e-4
+    gf = O.selective_scan_bwd(f["u"], f["delta"], f["A"], f["B"], f["C"], dout[..., :D], **kwf)
+    gr = O.selective_scan_bwd(r["u"], r["delta"], r["A"], r["B"], r["C"], dout[..., D:], **kwr)
+    names = ["du", "ddelta", "dA", "dB", "dC", "dD", "ddelta_bias"]
+    for name, t in zip(names, lf):
+        assert relerr(to_np(t.grad), gf[name]) < 1e-4, name
+    for name, t in zip(names, lr):
+        assert relerr(to_np(t.grad), gr[name]) < 1e-4, name
+    assert relerr(to_np(zt.grad), gf["dz"]) < 1e-4
+
+
 def test_empty_inputs(cuda):
     import selectssm_b200 as S
     for shape in [(0, 16, 32), (2, 0, 32)]:
