@@ -170,6 +170,37 @@ SSM_API size_t ssm_conv1d_workspace_bytes(const ssm_conv_params_t* p);
 SSM_API int ssm_conv1d_act_fwd(const ssm_conv_params_t* p, ssm_stream_t stream);
 SSM_API int ssm_conv1d_act_bwd(const ssm_conv_params_t* p, ssm_stream_t stream);
 
+/* ---- RMSNorm before the block and the residual base after it ----
+ * flax.linen.RMSNorm of BidirectionalMamba (selectssm.py:306-313, norm_type
+ * "rms"): y = x * rsqrt(mean(x^2) + eps) * scale over the last axis, plus, in
+ * the same pass, res_base = x + res_bias (the block's residual, selectssm.py
+ * :345-352, with out_proj's bias folded in) so that out_proj can accumulate
+ * onto it.  Rows of `dim` contiguous elements; scale, rstd, res_bias and
+ * dscale are fp32.  The backward writes dx (+ dres when given, the gradient
+ * reaching x through res_base) and dscale (summed in a fixed order). */
+typedef struct ssm_norm_params {
+  int64_t rows;                         /* number of rows (B * L) */
+  int32_t dim;                          /* 1 <= dim <= 1024 */
+  int32_t dtype;                        /* x, y, res_base, dy, dres, dx */
+  float eps;                            /* flax default 1e-6 */
+  const void* x;
+  const float* scale;                   /* (dim) */
+  void* y;                              /* forward output */
+  float* rstd;                          /* (rows) forward output, backward input */
+  const float* res_bias;                /* (dim) or NULL */
+  void* res_base;                       /* forward output x + res_bias, or NULL */
+  const void* dy;                       /* backward input: gradient of y */
+  const void* dres;                     /* backward input: gradient of res_base, or NULL */
+  void* dx;                             /* backward output */
+  float* dscale;                        /* backward output (dim) */
+  void* workspace;                      /* backward scratch: ssm_rmsnorm_workspace_bytes() */
+  size_t workspace_bytes;
+} ssm_norm_params_t;
+
+SSM_API size_t ssm_rmsnorm_workspace_bytes(const ssm_norm_params_t* p);
+SSM_API int ssm_rmsnorm_fwd(const ssm_norm_params_t* p, ssm_stream_t stream);
+SSM_API int ssm_rmsnorm_bwd(const ssm_norm_params_t* p, ssm_stream_t stream);
+
 /* Message for a status code (static storage). */
 SSM_API const char* ssm_strerror(int status);
 /* ---- backward without any device allocation ----

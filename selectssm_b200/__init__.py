@@ -8,7 +8,9 @@ conv preamble ``conv1d_act``.
 
 from .ops import (  # noqa: F401
     conv1d_act,
+    dense_onto,
     largest_factor_up_to,
+    rmsnorm_residual,
     selective_scan,
     selective_scan_bidir,
     ssm_chunked_scan,

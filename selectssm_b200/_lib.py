@@ -42,6 +42,7 @@ EXPORTED_SYMBOLS = (
     "ssm_workspace_bytes", "ssm_states_elems", "ssm_fwd", "ssm_bwd", "ssm_fwd_bidir", "ssm_bwd_bidir",
     "ssm_conv1d_workspace_bytes", "ssm_conv1d_act_fwd", "ssm_conv1d_act_bwd", "ssm_strerror", "ssm_last_error",
     "ssm_version", "ssm_bwd_noalloc", "ssm_launch_count",
+    "ssm_rmsnorm_workspace_bytes", "ssm_rmsnorm_fwd", "ssm_rmsnorm_bwd",
 )
 
 
@@ -81,6 +82,18 @@ class SSMConvParams(ctypes.Structure):
     ]
 
 
+class SSMNormParams(ctypes.Structure):
+    """Mirror of ``ssm_norm_params_t``."""
+
+    _fields_ = [
+        ("rows", ctypes.c_int64), ("dim", ctypes.c_int32), ("dtype", ctypes.c_int32), ("eps", ctypes.c_float),
+        ("x", ctypes.c_void_p), ("scale", ctypes.c_void_p), ("y", ctypes.c_void_p), ("rstd", ctypes.c_void_p),
+        ("res_bias", ctypes.c_void_p), ("res_base", ctypes.c_void_p), ("dy", ctypes.c_void_p),
+        ("dres", ctypes.c_void_p), ("dx", ctypes.c_void_p), ("dscale", ctypes.c_void_p),
+        ("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_size_t),
+    ]
+
+
 _lib = None
 
 
@@ -100,6 +113,7 @@ def load(path: str | None = None) -> ctypes.CDLL:
         raise SSMLibraryError(f"failed to load {p}: {e}") from e
     P = ctypes.POINTER(SSMParams)
     CP = ctypes.POINTER(SSMConvParams)
+    NP = ctypes.POINTER(SSMNormParams)
     sigs = {
         "ssm_workspace_bytes": (ctypes.c_size_t, [P]),
         "ssm_states_elems": (ctypes.c_size_t, [P]),
@@ -110,6 +124,9 @@ def load(path: str | None = None) -> ctypes.CDLL:
         "ssm_conv1d_workspace_bytes": (ctypes.c_size_t, [CP]),
         "ssm_conv1d_act_fwd": (ctypes.c_int, [CP, ctypes.c_void_p]),
         "ssm_conv1d_act_bwd": (ctypes.c_int, [CP, ctypes.c_void_p]),
+        "ssm_rmsnorm_workspace_bytes": (ctypes.c_size_t, [NP]),
+        "ssm_rmsnorm_fwd": (ctypes.c_int, [NP, ctypes.c_void_p]),
+        "ssm_rmsnorm_bwd": (ctypes.c_int, [NP, ctypes.c_void_p]),
         "ssm_strerror": (ctypes.c_char_p, [ctypes.c_int]),
         "ssm_last_error": (ctypes.c_char_p, []),
         "ssm_version": (ctypes.c_char_p, []),

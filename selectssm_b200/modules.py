@@ -298,7 +298,11 @@ class BidirectionalMamba(nn.Module):
 
     def forward(self, x, train: bool = False):
         skip = x                                                                 # :300
-        if self.norm_name is not None:
+        base = None
+        if self.norm_type == "rms":  # one kernel: the norm and the residual base skip + out_proj.bias
+            nm = getattr(self, self.norm_name)
+            x, base = ops.rmsnorm_residual(x, nm.scale, self.out_proj.bias, nm.eps)
+        elif self.norm_name is not None:
             nm = getattr(self, self.norm_name)
             x = nm(x, train) if self.norm_type == "batch" else nm(x)
         ED = self.ED
@@ -321,7 +325,10 @@ class BidirectionalMamba(nn.Module):
             g = sf(xf, train, z=zf, gate_act=self.activation) + sr(xr, train, z=zr, gate_act=self.activation)
         if "gated" in self.diagnostics and train:
             self.sown["gated_mean"], self.sown["gated_sd"] = g.mean(), g.std()
-        x = skip + self.out_proj(g)                                              # :345-352
+        if base is not None:                                                     # :345-352
+            x = ops.dense_onto(base, g, self.out_proj.kernel)  # base + g W: GEMM with the residual as accumulator
+        else:
+            x = skip + self.out_proj(g)
         if self.mlp_layer:                                                       # :355-362
             skip = x
             h = F.dropout(self.mlp(x), self.mlp_dropout_rate, training=train)

@@ -412,3 +412,69 @@ def conv1d_act(x, w, act="silu", reverse=False, complement=False):
     x: (B, L, D) in its own frame; w: Flax's ``shift_conv/kernel`` (K, 1, D) or
     (K, D).  u is in the scan frame (flipped when ``reverse``)."""
     return _Conv1dActFn.apply(x, w, act, bool(reverse), bool(complement))
+
+
+# ----------------------------------------------------------------------------- RMSNorm + residual base
+class _RMSNormResidualFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, scale, res_bias, eps):
+        _require_cuda(x, scale)
+        dim = x.shape[-1]
+        x2 = _dense(x).reshape(-1, dim)
+        scale = _dense(scale.float())
+        y = torch.empty_like(x2)
+        base = torch.empty_like(x2)
+        rstd = torch.empty(x2.shape[0], dtype=torch.float32, device=x.device)
+        p = _norm_params(x2, scale, eps, rstd)
+        bias = None if res_bias is None else _dense(res_bias.float())
+        p.y, p.res_base = y.data_ptr(), base.data_ptr()
+        p.res_bias = 0 if bias is None else bias.data_ptr()
+        _lib.check(_lib.load().ssm_rmsnorm_fwd(ctypes_byref(p), _stream()), "ssm_rmsnorm_fwd")
+        ctx.save_for_backward(x2, scale, rstd)
+        ctx.eps, ctx.shape, ctx.has_bias = eps, x.shape, res_bias is not None
+        return y.view(x.shape), base.view(x.shape)
+
+    @staticmethod
+    def backward(ctx, dy, dbase):
+        x2, scale, rstd = ctx.saved_tensors
+        dim = x2.shape[1]
+        dy = torch.zeros_like(x2) if dy is None else _dense(dy.to(x2.dtype)).reshape(-1, dim)
+        dres = None if dbase is None else _dense(dbase.to(x2.dtype)).reshape(-1, dim)
+        dx = torch.empty_like(x2)
+        dscale = torch.empty(dim, dtype=torch.float32, device=x2.device)
+        p = _norm_params(x2, scale, ctx.eps, rstd)
+        p.dy, p.dx, p.dscale = dy.data_ptr(), dx.data_ptr(), dscale.data_ptr()
+        p.dres = 0 if dres is None else dres.data_ptr()
+        lib = _lib.load()
+        ws = torch.empty(max(lib.ssm_rmsnorm_workspace_bytes(ctypes_byref(p)), 256), dtype=torch.uint8,
+                         device=x2.device)
+        p.workspace, p.workspace_bytes = ws.data_ptr(), ws.numel()
+        _lib.check(lib.ssm_rmsnorm_bwd(ctypes_byref(p), _stream()), "ssm_rmsnorm_bwd")
+        del ws
+        dbias = None
+        if ctx.has_bias:
+            dbias = torch.zeros(dim, dtype=torch.float32, device=x2.device) if dres is None else dres.float().sum(0)
+        return dx.view(ctx.shape), dscale, dbias, None
+
+
+def _norm_params(x2, scale, eps, rstd):
+    p = _lib.SSMNormParams()
+    p.rows, p.dim = x2.shape[0], x2.shape[1]
+    p.dtype = _dtype_code(x2)
+    p.eps = float(eps)
+    p.x, p.scale, p.rstd = x2.data_ptr(), scale.data_ptr(), rstd.data_ptr()
+    return p
+
+
+def rmsnorm_residual(x, scale, res_bias=None, eps=1e-6):
+    """flax.linen.RMSNorm of x over its last axis (selectssm.py:306-313) and, in
+    the same pass, the residual base x + res_bias of the block's output
+    (selectssm.py:345-352, with out_proj's bias folded in).  Returns (y, base)."""
+    return _RMSNormResidualFn.apply(x, scale, res_bias, float(eps))
+
+
+def dense_onto(base, h, kernel):
+    """base + h @ kernel in one cuBLAS call (the residual add of out_proj)."""
+    d = kernel.shape[1]
+    out = torch.addmm(base.reshape(-1, d), h.reshape(-1, h.shape[-1]), kernel.to(h.dtype))
+    return out.view(*h.shape[:-1], d)
