@@ -70,6 +70,8 @@ __device__ __forceinline__ void st_act(T* p, float v) {
 // Turns the per-segment adjoint aggregates into the adjoint entering each
 // segment from the right, in place: carry_{S-1} = 0,
 // carry_s = exp(A T_{s+1}) carry_{s+1} + F_{s+1}.  One thread per (b, d, n).
+// The loads of a batch of 8 segments are issued before the dependent chain
+// runs through them, so the chain waits on one load latency per batch.
 // Grid: (channel*state blocks, direction, batch row).
 __global__ void ssm_bwd_fold_kernel(const __grid_constant__ BwdLaunch P) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -78,14 +80,26 @@ __global__ void ssm_bwd_fold_kernel(const __grid_constant__ BwdLaunch P) {
   const int b = blockIdx.z;
   const int c = (int)(i / kN), n = (int)(i % kN);
   const float A2 = a.A[(size_t)c * kN + n] * kLog2e;
+  const size_t row0 = (size_t)b * a.nseg;
   float carry = 0.f;
-  for (int sg = a.nseg - 1; sg >= 0; --sg) {
-    const size_t r = (size_t)b * a.nseg + sg;
-    float* Fp = a.segF + (r * a.Dm + c) * kN + n;
-    const float F = sg > 0 ? *Fp : 0.f;
-    const float T = sg > 0 ? a.segT[r * a.Dm + c] : 0.f;
-    *Fp = carry;
-    carry = fmaf(ex2(A2 * T), carry, F);
+  constexpr int kBatch = 8;
+  for (int top = a.nseg - 1; top >= 0; top -= kBatch) {
+    float F[kBatch], T[kBatch];
+#pragma unroll
+    for (int k = 0; k < kBatch; ++k) {
+      const int sg = top - k;
+      const size_t r = row0 + (sg > 0 ? sg : 0);
+      F[k] = sg > 0 ? a.segF[(r * a.Dm + c) * kN + n] : 0.f;
+      T[k] = sg > 0 ? a.segT[r * a.Dm + c] : 0.f;
+    }
+#pragma unroll
+    for (int k = 0; k < kBatch; ++k) {
+      const int sg = top - k;
+      if (sg >= 0) {
+        a.segF[((row0 + sg) * a.Dm + c) * kN + n] = carry;
+        carry = fmaf(ex2(A2 * T[k]), carry, F[k]);
+      }
+    }
   }
 }
 
