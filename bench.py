@@ -125,10 +125,14 @@ class ClockSampler:
 
 
 # ----------------------------------------------------------------------------- inputs
-def host_inputs(seed, B, L, D, N):
-    """Seeded float32 host inputs of config 2 (one generator per tensor)."""
+def host_inputs(seed, B, L, D, N, bc_seed=None):
+    """Seeded float32 host inputs of config 2 (one generator per tensor).
+    bc_seed draws B and C from another seed (shared by channel shards)."""
     ss = np.random.SeedSequence(seed).spawn(8)
     g = [np.random.default_rng(s) for s in ss]
+    if bc_seed is not None:
+        sb = np.random.SeedSequence(bc_seed).spawn(8)
+        g[4], g[5] = np.random.default_rng(sb[4]), np.random.default_rng(sb[5])
     f32 = np.float32
     return dict(
         u=g[0].standard_normal((B, L, D), dtype=f32),
@@ -201,6 +205,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=8)
     ap.add_argument("--batch", type=int, default=None, help="override batch per GPU (small profiling cases)")
+    ap.add_argument("--parallel", default="batch", choices=["batch", "channels"],
+                    help="N>1 sharding: batch rows (default) or d_inner channels with B/C replicated")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -211,7 +217,10 @@ def main():
     Bsz, L, D, N = CFG["batch"], CFG["seqlen"], CFG["dim"], CFG["dstate"]
     config = {"workload": "config 2: raw selective-scan op fwd+bwd (softplus dt, D skip, silu gate fused)",
               "batch_per_gpu": Bsz, "global_batch": Bsz * world, "seq_len": L, "d_inner": D, "d_state": N,
-              "parallelism": f"batch-sharded dp{world}, NCCL all-reduce of dA/dD in bwd" if world > 1 else "single GPU",
+              "parallelism": ("single GPU" if world == 1 else
+                              f"batch-sharded dp{world}, NCCL all-reduce of dA/dD in bwd" if args.parallel == "batch"
+                              else f"d_inner-sharded x{world} ({D} channels per GPU), B/C replicated, "
+                                   "NCCL all-reduce of dB/dC in bwd"),
               "l2": "inputs larger than L2 (u, dt, z, dy = 805 MB per step), no flush"}
 
     if args.impl == "reference":
@@ -241,7 +250,7 @@ def main():
     import torch.distributed as dist
     import selectssm_b200 as S
     from selectssm_b200 import _lib
-    from selectssm_b200.parallel import allreduce_grads
+    from selectssm_b200.parallel import allreduce_grads, replicated_bc
 
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
@@ -249,7 +258,8 @@ def main():
         dist.init_process_group("nccl", device_id=dev)
     lib = _lib.load()
 
-    h = host_inputs(1234 + rank, Bsz, L, D, N)
+    chan = world > 1 and args.parallel == "channels"
+    h = host_inputs(1234 + rank, Bsz, L, D, N, bc_seed=1234 if chan else None)
     t = {k: torch.from_numpy(v).to(dev) for k, v in h.items()}
     for k in ("u", "delta", "z", "A", "B", "C", "D"):
         t[k].requires_grad_(True)
@@ -257,10 +267,13 @@ def main():
     def step(inputs):
         for k in ("u", "delta", "z", "A", "B", "C", "D"):
             inputs[k].grad = None
-        out = S.selective_scan(inputs["u"], inputs["delta"], inputs["A"], inputs["B"], inputs["C"], D=inputs["D"],
+        Bm, Cm = inputs["B"], inputs["C"]
+        if chan:  # channel sharding: the B / C gradients are summed over ranks in the backward
+            Bm, Cm = replicated_bc(Bm, Cm)
+        out = S.selective_scan(inputs["u"], inputs["delta"], inputs["A"], Bm, Cm, D=inputs["D"],
                                z=inputs["z"], delta_softplus=True)
         out.backward(inputs["dout"])
-        if world > 1:  # batch sharding: one all-reduce of the parameter gradients
+        if world > 1 and not chan:  # batch sharding: one all-reduce of the parameter gradients
             allreduce_grads([inputs["A"], inputs["D"]])
         return out
 

@@ -61,26 +61,33 @@ def shard_channels(x: torch.Tensor, rank: int = None, world_size: int = None, di
     return x.narrow(dim, s * multiple, (e - s) * multiple)
 
 
-class _SumGradAcrossRanks(torch.autograd.Function):
-    """Identity forward; the backward all-reduces (sums) the incoming gradient."""
+class _SumGradsAcrossRanks(torch.autograd.Function):
+    """Identity forward on several tensors; the backward sums their incoming
+    gradients over ranks with one all-reduce of a flattened buffer."""
 
     @staticmethod
-    def forward(ctx, x, group):
+    def forward(ctx, group, *xs):
         ctx.group = group
-        return x.view_as(x)
+        return tuple(x.view_as(x) for x in xs)
 
     @staticmethod
-    def backward(ctx, g):
-        g = g.contiguous()
-        if dist.is_initialized():
-            dist.all_reduce(g, op=dist.ReduceOp.SUM, group=ctx.group)
-        return g, None
+    def backward(ctx, *gs):
+        if not dist.is_initialized():
+            return (None,) + gs
+        flat = torch.cat([g.reshape(-1) for g in gs])
+        dist.all_reduce(flat, op=dist.ReduceOp.SUM, group=ctx.group)
+        out, off = [], 0
+        for g in gs:
+            out.append(flat[off:off + g.numel()].view_as(g))
+            off += g.numel()
+        return (None,) + tuple(out)
 
 
 def replicated_bc(Bm: torch.Tensor, Cm: torch.Tensor, group=None):
     """Mark B and C as replicated across a channel-sharded group: the gradients
-    each rank computes from its channels are summed over ranks."""
-    return _SumGradAcrossRanks.apply(Bm, group), _SumGradAcrossRanks.apply(Cm, group)
+    each rank computes from its channels are summed over ranks (one all-reduce
+    for both)."""
+    return _SumGradsAcrossRanks.apply(group, Bm, Cm)
 
 
 def allreduce_grads(params, group=None, average: bool = False):
