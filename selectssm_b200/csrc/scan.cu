@@ -216,9 +216,10 @@ struct SegPolicy {
   double agg_cost;  // pre-pass cost of one stage relative to the main kernel's
 };
 constexpr int kSMs = 148;
-// The forward's 64-thread CTAs are latency bound and share an SM well (up to 7
-// resident), so a "wave" is taken as the measured sweet spot of 1536 CTAs.
-constexpr SegPolicy kFwdSeg{kTileCh, 1536, 1536, 0.55};
+// The forward's CTAs are small and latency bound, so its "waves" are effective
+// sizes fitted to measurements (batch 8 runs best unsegmented with 384 CTAs,
+// batch 2 with 16 segments) rather than occupancy limits.
+constexpr SegPolicy kFwdSeg{kTileCh, 384, 768, 0.55};
 constexpr SegPolicy kBwdSeg{kBTile, 2L * kSMs, 4L * kSMs, 0.5};
 
 static Seg choose_segments(const Geo& g, SegPolicy pol) {
@@ -306,25 +307,25 @@ static int fill_fwd_dir(const ssm_params_t* p, const Geo& g, FwdDir* d) {
 
 template <typename T, typename TBC>
 static int launch_fwd_t(FwdLaunch& L, int ndir, const Geo& g, cudaStream_t s) {
-  using S = FwdSmem2<T, TBC>;
+  constexpr int kBytes = FwdSmem<T, TBC>::kBytes;
   const int nseg = L.dir[0].nseg;
   dim3 grid((g.Dm + kTileCh - 1) / kTileCh, g.B, 1);
   if (nseg > 1) {  // segment pre-pass: end state of every segment but the last
-    auto agg = ssm_fwd2_kernel<T, TBC, true, kFEmu>;
-    SSM_CUDA_CHECK(cudaFuncSetAttribute(agg, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kBytes),
+    auto agg = ssm_fwd_kernel<T, TBC, true>;
+    SSM_CUDA_CHECK(cudaFuncSetAttribute(agg, cudaFuncAttributeMaxDynamicSharedMemorySize, kBytes),
                    "cudaFuncSetAttribute(ssm_fwd_kernel<agg>)");
     L.zdiv = nseg - 1;
     grid.z = ndir * (nseg - 1);
-    agg<<<grid, kFThreads, S::kBytes, s>>>(L);
+    agg<<<grid, kFThreads, kBytes, s>>>(L);
     note_launches(1);
   SSM_CUDA_CHECK(cudaGetLastError(), "launch ssm_fwd_kernel<agg>");
   }
-  auto kern = ssm_fwd2_kernel<T, TBC, false, kFEmu>;
-  SSM_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kBytes),
+  auto kern = ssm_fwd_kernel<T, TBC, false>;
+  SSM_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kBytes),
                  "cudaFuncSetAttribute(ssm_fwd_kernel)");
   L.zdiv = nseg;
   grid.z = ndir * nseg;
-  kern<<<grid, kFThreads, S::kBytes, s>>>(L);
+  kern<<<grid, kFThreads, kBytes, s>>>(L);
   note_launches(1);
   SSM_CUDA_CHECK(cudaGetLastError(), "launch ssm_fwd_kernel");
   return SSM_OK;

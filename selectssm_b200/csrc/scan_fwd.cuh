@@ -1,21 +1,21 @@
-// Selective-scan forward kernel for B200 (sm_100a), lane-pair design.
+// Selective-scan forward kernel for B200 (sm_100a).
 //
 // Work decomposition
 //   CTA   = one batch row b x 32 consecutive channels x one sequence segment;
-//           2 warps of 16 channels.  A channel belongs to a lane pair
-//           (lane = 2 ch + half); each lane owns 8 of the 16 states
-//           (n = 8 half .. 8 half + 7) as 4 packed f32x2 pairs.
+//           4 warps of 8 channels.  A channel belongs to 4 lanes
+//           (lane = 4 ch + nq), each owning 4 of the 16 states
+//           (n = 4 nq .. 4 nq + 3) as 2 packed f32x2 pairs.
 //   time  = TMA stages of 16 steps (u, delta, z tiles of 32 ch x 16 steps, the
 //           B and C tiles of 16 steps x 16 states) in a ring of shared-memory
 //           stages completed on mbarriers, issued STAGES-1 stages ahead.
 //   Per stage, each lane evaluates the per-step scalars softplus(dt + bias) and
-//   dt x for the 8 steps of its parity (t = 2 i + half) and the pair swaps them
-//   with one shuffle each per step.  y_t = C_t . h_t is half on each lane; one
-//   shuffle per two steps both completes it and hands step 2i to half 0 and
-//   step 2i+1 to half 1, which run the epilogue (D skip, gate, store) for the
-//   steps they own.
-//   alpha = 2^(A log2(e) dt) uses the MUFU unit for 4 - EMU pairs and the FMA
-//   pipe (ex2_poly2) for EMU pairs, so the two units share the exponentials.
+//   dt x for 4 of the 16 steps (t = 4 i + nq) and the quad swaps them with
+//   shuffles.  y_t = C_t . h_t is a quarter on each lane; every 4 steps a
+//   reduce-scatter over the quad (3 shuffles) leaves step 4 i + nq's total on
+//   lane nq, which runs that step's epilogue (D skip, gate, store).  The gate
+//   activation is dispatched once per stage, so the step loops hold no branch.
+//   Four lanes per channel give 4x the warps of a lane-per-channel layout,
+//   enough to fill the GPU at batch 8 without cutting the sequence.
 //
 // Recurrence (src/selectssm/selectssm.py:74-78, :90): h_t = exp(A dt_t) h_{t-1}
 // + dt_t B_t x_t, y_t = C_t . h_t; then the D skip (:238), the reverse /
@@ -34,12 +34,13 @@
 
 namespace ssm {
 
-constexpr int kFThreads = 64;      // 2 warps x 16 channels = kTileCh
+
+
+constexpr int kFThreads = 128;  // 4 warps x 8 channels = kTileCh
 constexpr int kFStages = 3;
-constexpr int kFEmu = 1;           // state pairs per lane whose exponential runs on the FMA pipe
 
 template <typename T, typename TBC>
-struct FwdSmem2 {
+struct FwdSmem {
   static constexpr int kAct = kChunk * kTileCh * (int)sizeof(T);
   static constexpr int kBC = kChunk * kN * (int)sizeof(TBC);
   static constexpr int kOffU = 0, kOffDelta = kAct, kOffZ = 2 * kAct, kOffUo = 3 * kAct;
@@ -49,18 +50,10 @@ struct FwdSmem2 {
   static constexpr int kBytes = kBars + 8 * kFStages;
 };
 
-template <typename TB>
-__device__ __forceinline__ void ld8(const TB* row, float2 (&v)[4]) {
-  const float4 a = ld4(row), b = ld4(row + 4);
-  v[0] = make_float2(a.x, a.y);
-  v[1] = make_float2(a.z, a.w);
-  v[2] = make_float2(b.x, b.y);
-  v[3] = make_float2(b.z, b.w);
-}
 
-template <typename T, typename TBC, bool AGG, int EMU>
-__global__ void __launch_bounds__(kFThreads, 8) ssm_fwd2_kernel(const __grid_constant__ FwdLaunch P) {
-  using S = FwdSmem2<T, TBC>;
+template <typename T, typename TBC, bool AGG>
+__global__ void __launch_bounds__(kFThreads, 6) ssm_fwd_kernel(const __grid_constant__ FwdLaunch P) {
+  using S = FwdSmem<T, TBC>;
   const FwdDir& a = P.dir[blockIdx.z / P.zdiv];
   const int seg = blockIdx.z % P.zdiv;
   extern __shared__ __align__(1024) unsigned char smem[];
@@ -69,11 +62,11 @@ __global__ void __launch_bounds__(kFThreads, 8) ssm_fwd2_kernel(const __grid_con
   const int b = blockIdx.y;
   const int c0 = blockIdx.x * kTileCh;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int half = lane & 1;
-  const int cl = warp * 16 + (lane >> 1);
+  const int nq = lane & 3;
+  const int cl = warp * 8 + (lane >> 2);
   const int c = c0 + cl;
   const int L = a.L, Dm = a.Dm;
-  if (c0 >= Dm) return;  // grid is sized for the larger direction
+  if (c0 >= Dm) return;
   const bool rev = (a.flags & SSM_REVERSE) != 0;
   const bool comp = rev && (a.flags & SSM_COMPLEMENT);
   const bool aligned = (a.flags & SSM_ALIGNED_SKIP) != 0;
@@ -86,8 +79,8 @@ __global__ void __launch_bounds__(kFThreads, 8) ssm_fwd2_kernel(const __grid_con
   const int j1 = min(nblk, j0 + a.seg_chunks);
   const int nloc = j1 - j0;
   const bool cvalid = c < Dm;
-  const int co = comp ? Dm - 1 - c : c;              // output-frame channel
-  const int oc0 = comp ? Dm - kTileCh - c0 : c0;     // output-frame tile start
+  const int co = comp ? Dm - 1 - c : c;
+  const int oc0 = comp ? Dm - kTileCh - c0 : c0;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kFStages; ++s) mbar_init(&bars[s], 1);
@@ -97,7 +90,7 @@ __global__ void __launch_bounds__(kFThreads, 8) ssm_fwd2_kernel(const __grid_con
 
   const uint32_t tx = AGG ? 2 * S::kAct + S::kBC
                           : 2 * S::kAct + 2 * S::kBC + (has_z ? S::kAct : 0) + (need_uo ? S::kAct : 0);
-  auto issue = [&](int jl) {  // local stage index within the segment
+  auto issue = [&](int jl) {
     unsigned char* st = smem + (jl % kFStages) * S::kStage;
     uint64_t* bar = &bars[jl % kFStages];
     const int t0 = (j0 + jl) * kChunk;
@@ -117,39 +110,29 @@ __global__ void __launch_bounds__(kFThreads, 8) ssm_fwd2_kernel(const __grid_con
     for (int jl = 0; jl < npre; ++jl) issue(jl);
   }
 
-  // per-lane constants: A log2(e) of this lane's 8 states
-  float2 A2[4];
+  float2 A2[2];
   {
-    float4 a0 = make_float4(0.f, 0.f, 0.f, 0.f), a1 = a0;
-    if (cvalid) {
-      a0 = *reinterpret_cast<const float4*>(a.A + (size_t)c * kN + half * 8);
-      a1 = *reinterpret_cast<const float4*>(a.A + (size_t)c * kN + half * 8 + 4);
-    }
-    A2[0] = make_float2(a0.x * kLog2e, a0.y * kLog2e);
-    A2[1] = make_float2(a0.z * kLog2e, a0.w * kLog2e);
-    A2[2] = make_float2(a1.x * kLog2e, a1.y * kLog2e);
-    A2[3] = make_float2(a1.z * kLog2e, a1.w * kLog2e);
+    const float4 v = cvalid ? *reinterpret_cast<const float4*>(a.A + (size_t)c * kN + 4 * nq)
+                            : make_float4(0.f, 0.f, 0.f, 0.f);
+    A2[0] = make_float2(v.x * kLog2e, v.y * kLog2e);
+    A2[1] = make_float2(v.z * kLog2e, v.w * kLog2e);
   }
   const float bias = (a.bias && cvalid) ? a.bias[c] : 0.f;
   const float Dsk = (has_D && cvalid) ? a.D[aligned ? c : co] : 0.f;
-  float2 h[4];
-#pragma unroll
-  for (int p = 0; p < 4; ++p) h[p] = make_float2(0.f, 0.f);
+  float2 h[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
   if (!AGG && cvalid) {  // fold the end states of the preceding segments
     for (int sp = 0; sp < seg; ++sp) {
       const size_t r = (size_t)b * a.nseg + sp;
       const float Tsum = a.segT[r * Dm + c];
-      float2 H[4];
-      ld8(a.segH + (r * Dm + c) * kN + half * 8, H);
-#pragma unroll
-      for (int p = 0; p < 4; ++p) {
-        const float2 e = fmul2(A2[p], dup2(Tsum));
-        h[p] = ffma2(make_float2(ex2(e.x), ex2(e.y)), h[p], H[p]);
-      }
+      const float4 H = *reinterpret_cast<const float4*>(a.segH + (r * Dm + c) * kN + 4 * nq);
+      const float2 e0 = fmul2(A2[0], dup2(Tsum)), e1 = fmul2(A2[1], dup2(Tsum));
+      h[0] = ffma2(make_float2(ex2(e0.x), ex2(e0.y)), h[0], make_float2(H.x, H.y));
+      h[1] = ffma2(make_float2(ex2(e1.x), ex2(e1.y)), h[1], make_float2(H.z, H.w));
     }
   }
-  float tsum = 0.f;  // AGG: sum of dt over this lane's steps
+  float tsum = 0.f;
   T* out = reinterpret_cast<T*>(a.out);
+  const bool b1 = (nq & 2) != 0, b0 = (nq & 1) != 0;
 
   for (int j = j0; j < j1; ++j) {
     const int jl = j - j0;
@@ -162,14 +145,13 @@ __global__ void __launch_bounds__(kFThreads, 8) ssm_fwd2_kernel(const __grid_con
     const unsigned char* st = smem + s * S::kStage;
     const T* su = reinterpret_cast<const T*>(st + S::kOffU);
     const T* sd = reinterpret_cast<const T*>(st + S::kOffDelta);
-    const TBC* sB = reinterpret_cast<const TBC*>(st + S::kOffB);
-    const TBC* sC = reinterpret_cast<const TBC*>(st + S::kOffC);
+    const TBC* sB = reinterpret_cast<const TBC*>(st + S::kOffB) + 4 * nq;
+    const TBC* sC = reinterpret_cast<const TBC*>(st + S::kOffC) + 4 * nq;
 
-    // per-step scalars of this lane's 8 steps (tl = 2 i + half)
-    float dtv[8], dxv[8];
+    float dtv[4], dxv[4];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const int tl = 2 * i + half;
+    for (int i = 0; i < 4; ++i) {
+      const int tl = 4 * i + nq;
       const bool valid = j * kChunk + tl < L;
       const float x = ld_f(su + tl * kTileCh + cl);
       const float dr = ld_f(sd + tl * kTileCh + cl) + bias;
@@ -180,56 +162,54 @@ __global__ void __launch_bounds__(kFThreads, 8) ssm_fwd2_kernel(const __grid_con
       tsum += dt;
     }
 
-    float yv[8];
-    float yeven = 0.f;
+    float yv[4];
 #pragma unroll
-    for (int tl = 0; tl < kChunk; ++tl) {
-      const int src = (lane & ~1) | (tl & 1);
-      const float dt = __shfl_sync(kFull, dtv[tl >> 1], src);
-      const float dx = __shfl_sync(kFull, dxv[tl >> 1], src);
-      float2 Bq[4];
-      ld8(sB + tl * kN + half * 8, Bq);
-      const float2 dt2 = dup2(dt), dx2 = dup2(dx);
-      float2 alpha[4];
+    for (int i = 0; i < 4; ++i) {  // 4 steps per group, reduce-scattered over the quad
+      float yp[4];
 #pragma unroll
-      for (int p = 0; p < 4; ++p) {
-        const float2 e = fmul2(A2[p], dt2);
-        alpha[p] = p < EMU ? ex2_poly2(e) : make_float2(ex2(e.x), ex2(e.y));
-      }
-#pragma unroll
-      for (int p = 0; p < 4; ++p) h[p] = ffma2(alpha[p], h[p], fmul2(Bq[p], dx2));
-      if (!AGG) {
-        float2 Cq[4];
-        ld8(sC + tl * kN + half * 8, Cq);
-        float2 y2 = fmul2(Cq[0], h[0]);
-#pragma unroll
-        for (int p = 1; p < 4; ++p) y2 = ffma2(Cq[p], h[p], y2);
-        const float yp = y2.x + y2.y;
-        if ((tl & 1) == 0) {
-          yeven = yp;
-        } else {  // half 0 keeps step tl-1, half 1 keeps step tl
-          const float mine = half ? yp : yeven, other = half ? yeven : yp;
-          yv[tl >> 1] = mine + __shfl_xor_sync(kFull, other, 1);
-        }
-        if ((tl & (kCk - 1)) == kCk - 1) {  // checkpoint after every kCk steps
-          const int ck = j * (kChunk / kCk) + tl / kCk;
-          if (cvalid && ck < nck) {
-            float4* sp = reinterpret_cast<float4*>(a.states + (((size_t)b * nck + ck) * Dm + c) * kN + half * 8);
-            sp[0] = make_float4(h[0].x, h[0].y, h[1].x, h[1].y);
-            sp[1] = make_float4(h[2].x, h[2].y, h[3].x, h[3].y);
+      for (int k = 0; k < 4; ++k) {
+        const int tl = 4 * i + k;
+        const int src = (lane & ~3) | k;
+        const float dt = __shfl_sync(kFull, dtv[i], src);
+        const float dx = __shfl_sync(kFull, dxv[i], src);
+        const float4 Bv = ld4(sB + tl * kN);
+        const float2 dt2 = dup2(dt), dx2 = dup2(dx);
+        const float2 e0 = fmul2(A2[0], dt2), e1 = fmul2(A2[1], dt2);
+        const float2 al0 = make_float2(ex2(e0.x), ex2(e0.y));
+        const float2 al1 = make_float2(ex2(e1.x), ex2(e1.y));
+        h[0] = ffma2(al0, h[0], fmul2(make_float2(Bv.x, Bv.y), dx2));
+        h[1] = ffma2(al1, h[1], fmul2(make_float2(Bv.z, Bv.w), dx2));
+        if (!AGG) {
+          const float4 Cv = ld4(sC + tl * kN);
+          const float2 y2 = ffma2(make_float2(Cv.z, Cv.w), h[1], fmul2(make_float2(Cv.x, Cv.y), h[0]));
+          yp[k] = y2.x + y2.y;
+          if ((tl & (kCk - 1)) == kCk - 1) {  // checkpoint after every kCk steps
+            const int ck = j * (kChunk / kCk) + tl / kCk;
+            if (cvalid && ck < nck)
+              *reinterpret_cast<float4*>(a.states + (((size_t)b * nck + ck) * Dm + c) * kN + 4 * nq) =
+                  make_float4(h[0].x, h[0].y, h[1].x, h[1].y);
           }
         }
       }
+      if (!AGG) {
+        // lane bit 1: keep steps {0,1} or {2,3}; lane bit 0: keep one of the two
+        const float k0 = b1 ? yp[2] : yp[0], k1 = b1 ? yp[3] : yp[1];
+        const float s0 = b1 ? yp[0] : yp[2], s1 = b1 ? yp[1] : yp[3];
+        const float r0 = k0 + __shfl_xor_sync(kFull, s0, 2);
+        const float r1 = k1 + __shfl_xor_sync(kFull, s1, 2);
+        const float kk = b0 ? r1 : r0, ss = b0 ? r0 : r1;
+        yv[i] = kk + __shfl_xor_sync(kFull, ss, 1);  // total of step 4 i + nq
+      }
     }
 
-    if (!AGG) {  // epilogue: skip, gate, store (this lane's 8 steps); gate chosen once per stage
+    if (!AGG) {  // epilogue of this lane's steps (t = 4 i + nq); gate chosen once per stage
       const T* sz = reinterpret_cast<const T*>(st + S::kOffZ);
       const T* suo = reinterpret_cast<const T*>(st + S::kOffUo);
       auto epilogue = [&](auto gate) {
-        constexpr int G = decltype(gate)::value;  // -1: no z, else an ssm_act code
+        constexpr int G = decltype(gate)::value;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const int tl = 2 * i + half;
+        for (int i = 0; i < 4; ++i) {
+          const int tl = 4 * i + nq;
           const int t = j * kChunk + tl;
           const int row = rev ? kChunk - 1 - tl : tl;
           const int col = comp ? kTileCh - 1 - cl : cl;
@@ -248,7 +228,7 @@ __global__ void __launch_bounds__(kFThreads, 8) ssm_fwd2_kernel(const __grid_con
         default: epilogue(std::integral_constant<int, SSM_ACT_NONE>{}); break;
       }
     }
-    __syncthreads();  // both warps are done with stage s
+    __syncthreads();
     if (threadIdx.x == 0 && jl + kFStages < nloc) {
       fence_proxy_async_smem();
       issue(jl + kFStages);
@@ -256,12 +236,11 @@ __global__ void __launch_bounds__(kFThreads, 8) ssm_fwd2_kernel(const __grid_con
   }
   if (AGG) {
     tsum += __shfl_xor_sync(kFull, tsum, 1);
+    tsum += __shfl_xor_sync(kFull, tsum, 2);
     if (cvalid) {
       const size_t r = (size_t)b * a.nseg + seg;
-      float4* hp = reinterpret_cast<float4*>(a.segH + (r * Dm + c) * kN + half * 8);
-      hp[0] = make_float4(h[0].x, h[0].y, h[1].x, h[1].y);
-      hp[1] = make_float4(h[2].x, h[2].y, h[3].x, h[3].y);
-      if (half == 0) a.segT[r * Dm + c] = tsum;
+      *reinterpret_cast<float4*>(a.segH + (r * Dm + c) * kN + 4 * nq) = make_float4(h[0].x, h[0].y, h[1].x, h[1].y);
+      if (nq == 0) a.segT[r * Dm + c] = tsum;
     }
   }
 }
