@@ -201,6 +201,12 @@ SSM_API size_t ssm_rmsnorm_workspace_bytes(const ssm_norm_params_t* p);
 SSM_API int ssm_rmsnorm_fwd(const ssm_norm_params_t* p, ssm_stream_t stream);
 SSM_API int ssm_rmsnorm_bwd(const ssm_norm_params_t* p, ssm_stream_t stream);
 
+/* Failure-path self-test: one tiny kernel waits, with the scan kernels'
+ * bounded wait, on an mbarrier that nothing arrives on; after spin_limit polls
+ * (1 .. 2^24) it writes SSM_ERR_TIMEOUT to *status (a device int32) and
+ * returns, leaving the context usable.  No counterpart in the reference. */
+SSM_API int ssm_selftest_wait_timeout(int32_t* status, uint32_t spin_limit, ssm_stream_t stream);
+
 /* Message for a status code (static storage). */
 SSM_API const char* ssm_strerror(int status);
 /* ---- backward without any device allocation ----

@@ -42,7 +42,7 @@ EXPORTED_SYMBOLS = (
     "ssm_workspace_bytes", "ssm_states_elems", "ssm_fwd", "ssm_bwd", "ssm_fwd_bidir", "ssm_bwd_bidir",
     "ssm_conv1d_workspace_bytes", "ssm_conv1d_act_fwd", "ssm_conv1d_act_bwd", "ssm_strerror", "ssm_last_error",
     "ssm_version", "ssm_bwd_noalloc", "ssm_launch_count",
-    "ssm_rmsnorm_workspace_bytes", "ssm_rmsnorm_fwd", "ssm_rmsnorm_bwd",
+    "ssm_rmsnorm_workspace_bytes", "ssm_rmsnorm_fwd", "ssm_rmsnorm_bwd", "ssm_selftest_wait_timeout",
 )
 
 
@@ -127,6 +127,7 @@ def load(path: str | None = None) -> ctypes.CDLL:
         "ssm_rmsnorm_workspace_bytes": (ctypes.c_size_t, [NP]),
         "ssm_rmsnorm_fwd": (ctypes.c_int, [NP, ctypes.c_void_p]),
         "ssm_rmsnorm_bwd": (ctypes.c_int, [NP, ctypes.c_void_p]),
+        "ssm_selftest_wait_timeout": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_uint32, ctypes.c_void_p]),
         "ssm_strerror": (ctypes.c_char_p, [ctypes.c_int]),
         "ssm_last_error": (ctypes.c_char_p, []),
         "ssm_version": (ctypes.c_char_p, []),
