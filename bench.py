@@ -199,7 +199,7 @@ def run_cpu_sample(seqlen=4096, reps=1, warm_seqlen=256):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=300)
+    ap.add_argument("--steps", type=int, default=1000)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -228,11 +228,13 @@ def main():
             return
         steps = max(1, args.steps)
         vals = []
+        # each step times the oracle on one batch row of L=64 (about 0.1 s on the
+        # host cores), so the default 1000 steps finish within about two minutes
         for _ in range(args.warmup):
-            run_cpu_sample(seqlen=64, warm_seqlen=64)
+            run_cpu_sample(seqlen=64, warm_seqlen=16)
         t0 = time.perf_counter()
         for _ in range(steps):
-            v, _, sample = run_cpu_sample(seqlen=128, warm_seqlen=16)
+            v, _, sample = run_cpu_sample(seqlen=64, warm_seqlen=16)
             vals.append(v)
         total = time.perf_counter() - t0
         v = statistics.median(vals)
