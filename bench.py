@@ -266,6 +266,8 @@ def main():
     for k in ("u", "delta", "z", "A", "B", "C", "D"):
         t[k].requires_grad_(True)
 
+    pending = []
+
     def step(inputs):
         for k in ("u", "delta", "z", "A", "B", "C", "D"):
             inputs[k].grad = None
@@ -275,12 +277,18 @@ def main():
         out = S.selective_scan(inputs["u"], inputs["delta"], inputs["A"], Bm, Cm, D=inputs["D"],
                                z=inputs["z"], delta_softplus=True)
         out.backward(inputs["dout"])
-        if world > 1 and not chan:  # batch sharding: one all-reduce of the parameter gradients
-            allreduce_grads([inputs["A"], inputs["D"]])
+        if world > 1 and not chan:  # batch sharding: one all-reduce of the parameter gradients,
+            finish_reduce()            # overlapped with the next step's forward
+            pending.append(allreduce_grads([inputs["A"], inputs["D"]], async_op=True))
         return out
+
+    def finish_reduce():
+        while pending:
+            pending.pop().wait()
 
     for _ in range(max(3, args.warmup)):
         step(t)
+    finish_reduce()
     torch.cuda.synchronize()
     stream = torch.cuda.current_stream()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -293,6 +301,7 @@ def main():
         e0.record(stream)
         for _ in range(args.steps):
             step(t)
+        finish_reduce()
         e1.record(stream)
         n_launches = lib.ssm_launch_count() - n_launch0
         torch.cuda.synchronize()
@@ -394,6 +403,7 @@ def main():
     torch.cuda.synchronize()
     ee0.record(stream)
     pipeline(args.e2e_steps)
+    finish_reduce()
     ee1.record(stream)
     torch.cuda.synchronize()
     ems = ee0.elapsed_time(ee1) / args.e2e_steps

@@ -90,18 +90,39 @@ def replicated_bc(Bm: torch.Tensor, Cm: torch.Tensor, group=None):
     return _SumGradsAcrossRanks.apply(group, Bm, Cm)
 
 
-def allreduce_grads(params, group=None, average: bool = False):
+class _PendingReduce:
+    """An all-reduce in flight; wait() makes the current stream wait for it and
+    copies the reduced values into the gradient tensors captured at the call
+    (the parameters' .grad at that time)."""
+
+    def __init__(self, work, flat, grads, scale):
+        self.work, self.flat, self.grads, self.scale = work, flat, grads, scale
+
+    def wait(self):
+        if self.work is not None:
+            self.work.wait()
+        if self.scale is not None:
+            self.flat /= self.scale
+        off = 0
+        for g in self.grads:
+            n = g.numel()
+            g.copy_(self.flat[off:off + n].view_as(g))
+            off += n
+
+
+def allreduce_grads(params, group=None, average: bool = False, async_op: bool = False):
     """Sum (or average) the .grad of ``params`` over ranks with a single
-    all-reduce of one flattened buffer (batch sharding)."""
+    all-reduce of one flattened buffer (batch sharding).  With async_op the
+    reduction overlaps whatever the caller launches next; the returned handle's
+    wait() finishes it (stream-ordered) and writes the results back."""
     ps = [p for p in params if p.grad is not None]
     if not ps or not dist.is_initialized():
-        return
+        return None
     flat = torch.cat([p.grad.reshape(-1) for p in ps])
-    dist.all_reduce(flat, op=dist.ReduceOp.SUM, group=group)
-    if average:
-        flat /= dist.get_world_size(group)
-    off = 0
-    for p in ps:
-        n = p.grad.numel()
-        p.grad.copy_(flat[off:off + n].view_as(p.grad))
-        off += n
+    work = dist.all_reduce(flat, op=dist.ReduceOp.SUM, group=group, async_op=async_op)
+    pending = _PendingReduce(work if async_op else None, flat, [p.grad for p in ps],
+                             dist.get_world_size(group) if average else None)
+    if async_op:
+        return pending
+    pending.wait()
+    return None

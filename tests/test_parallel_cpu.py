@@ -58,7 +58,17 @@ def _batch_worker(rank, world, port, q):
         for p, k in zip(params, ("dA", "dD", "ddelta_bias")):
             p.grad = torch.from_numpy(g[k].copy())
         allreduce_grads(params)
-        q.put((rank, [p.grad.numpy() for p in params]))
+        sync = [p.grad.numpy().copy() for p in params]
+        # the asynchronous form writes the same sums into the gradients captured at the call
+        grads = [torch.from_numpy(g[k].copy()) for k in ("dA", "dD", "ddelta_bias")]
+        for p, gr in zip(params, grads):
+            p.grad = gr
+        handle = allreduce_grads(params, async_op=True)
+        for p in params:
+            p.grad = None  # the caller may move on before waiting
+        handle.wait()
+        assert all(np.array_equal(a, b.numpy()) for a, b in zip(sync, grads))
+        q.put((rank, sync))
         dist.destroy_process_group()
     except Exception as ex:  # pragma: no cover - reported to the parent
         q.put((rank, repr(ex)))
