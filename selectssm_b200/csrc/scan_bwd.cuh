@@ -24,6 +24,14 @@
 //   The 4 warps' partials are summed in shared memory and added over channel
 //   tiles with 16-byte atomics.  dA/dD/d(delta_bias) are per-(batch row,
 //   segment) partials summed in a fixed order by the finalize kernel.
+//   The gate activation is a template parameter (fixed per launch) and the
+//   per-step work holds no data- or flag-dependent branch (only stores are
+//   predicated), so the compiler can schedule across the unrolled steps.
+// Segments: ssm_bwd_agg_kernel runs segments 1..S-1 from a zero adjoint and
+//   writes the adjoint carried out of each one's first step (one lane per
+//   channel, 16 states; one state pair per lane evaluates its exponential on
+//   the FMA pipe to relieve the MUFU unit); ssm_bwd_fold_kernel turns those
+//   into the carry entering each segment.
 #pragma once
 
 #include "scan_kernels.cuh"
