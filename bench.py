@@ -203,7 +203,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--e2e-steps", type=int, default=8)
+    ap.add_argument("--e2e-steps", type=int, default=20)
     ap.add_argument("--batch", type=int, default=None, help="override batch per GPU (small profiling cases)")
     ap.add_argument("--parallel", default="batch", choices=["batch", "channels"],
                     help="N>1 sharding: batch rows (default) or d_inner channels with B/C replicated")
