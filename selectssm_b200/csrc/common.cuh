@@ -184,6 +184,32 @@ __device__ __forceinline__ float act_grad_f(float x, int act) {
   }
 }
 
+// act(x) and act'(x) together, sharing the exponential / tanh
+__device__ __forceinline__ void act_and_grad(float x, int act, float& a, float& g) {
+  switch (act) {
+    case 1: {
+      const float s = sigmoid_f(x);
+      a = x * s;
+      g = s * (1.f + x * (1.f - s));
+      return;
+    }
+    case 2: {
+      const float t = tanh_f(kGeluC * (x + 0.044715f * x * x * x));
+      const float di = kGeluC * (1.f + 3.f * 0.044715f * x * x);
+      a = 0.5f * x * (1.f + t);
+      g = 0.5f * (1.f + t) + 0.5f * x * (1.f - t * t) * di;
+      return;
+    }
+    case 3:
+      a = fmaxf(x, 0.f);
+      g = x > 0.f ? 1.f : 0.f;
+      return;
+    default:
+      a = x;
+      g = 1.f;
+  }
+}
+
 // ---------------------------------------------------------------- packed fp32 (sm_100 f32x2)
 __device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
   float2 d;

@@ -210,16 +210,12 @@ __global__ void __launch_bounds__(kBThreads, 2) ssm_bwd_kernel(const __grid_cons
   const bool b2 = ((lane >> 2) & 1) != 0, b1 = ((lane >> 1) & 1) != 0;
   const int red_n = 4 * xq + (b2 ? 2 : 0) + (b1 ? 1 : 0);
   const bool red_writer = (lane & 1) == 0;
-  float2 An[8];
-  {
-    const float* Ar = a.A + (size_t)(cvalid ? c : 0) * kN;
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const float4 f = cvalid ? *reinterpret_cast<const float4*>(Ar + 4 * (q ^ xq)) : make_float4(0.f, 0.f, 0.f, 0.f);
-      An[2 * q] = make_float2(f.x, f.y);
-      An[2 * q + 1] = make_float2(f.z, f.w);
-    }
-  }
+  // A (pairs at the permuted quad addresses) is re-read from L1 at each use
+  // rather than held in 16 registers.
+  const float* Arow = a.A + (size_t)(cvalid ? c : 0) * kN;
+  auto An_at = [&](int p) {
+    return __ldg(reinterpret_cast<const float2*>(Arow + 4 * ((p >> 1) ^ xq) + 2 * (p & 1)));
+  };
   const float bias = (a.bias && cvalid) ? a.bias[c] : 0.f;
   const float Dsc = (has_D && cvalid) ? a.D[c] : 0.f;                  // skip weight, scan channel
   const float Dso = (has_D && cvalid) ? a.D[aligned ? c : co] : 0.f;   // skip weight in the pre-gate value
@@ -262,7 +258,8 @@ __global__ void __launch_bounds__(kBThreads, 2) ssm_bwd_kernel(const __grid_cons
       // ---- per-step scalars of the block (own channel)
       // (sgv: upstream gradient of the skip term in the scan frame; it differs
       // from dyv only for the reference's reverse-skip frame)
-      float dtv[kCk], dxv[kCk], dyv[kCk], sgv[kCk];
+      // (zgv: act'(z) of the step, for dz)
+      float dtv[kCk], dxv[kCk], dyv[kCk], sgv[kCk], zgv[kCk];
 #pragma unroll
       for (int u = 0; u < kCk; ++u) {
         const int tl = T0 + u;
@@ -274,7 +271,12 @@ __global__ void __launch_bounds__(kBThreads, 2) ssm_bwd_kernel(const __grid_cons
         dxv[u] = valid ? dt * x : 0.f;
         const int row = rev ? kChunk - 1 - tl : tl;
         float g = ld_f(sdo + row * kBTile);
-        if (has_z) g *= act_f(ld_f(szo + row * kBTile), G);
+        zgv[u] = 1.f;
+        if (has_z) {
+          float av;
+          act_and_grad(ld_f(szo + row * kBTile), G, av, zgv[u]);
+          g *= av;
+        }
         dyv[u] = valid ? g : 0.f;
         sgv[u] = dyv[u];
       }
@@ -307,7 +309,7 @@ __global__ void __launch_bounds__(kBThreads, 2) ssm_bwd_kernel(const __grid_cons
         float2 y2 = make_float2(0.f, 0.f), vc[8];
 #pragma unroll
         for (int p = 0; p < 8; ++p) {
-          const float2 e = fmul2(An[p], dt2);
+          const float2 e = fmul2(An_at(p), dt2);
           const float2 al = make_float2(ex2(e.x), ex2(e.y));
           const float2 q = fmul2(al, h[p]);
           h[p] = ffma2(Bq[p], dx2, q);
@@ -328,7 +330,7 @@ __global__ void __launch_bounds__(kBThreads, 2) ssm_bwd_kernel(const __grid_cons
           const int l = rev ? L - 1 - t : t;
           const float xs = ld_f(mirror ? suo + row * kBTile : su + tl * kBTile);
           const float pre = fmaf(Dso, xs, y2.x + y2.y);  // Dso is 0 without a skip
-          const float g = ld_f(sdo + row * kBTile) * pre * act_grad_f(ld_f(szo + row * kBTile), G);
+          const float g = ld_f(sdo + row * kBTile) * pre * zgv[u];
           if (t < L && cvalid) st_act(dz_g + (size_t)l * a.z_stride, g);
         }
       }
@@ -355,7 +357,7 @@ __global__ void __launch_bounds__(kBThreads, 2) ssm_bwd_kernel(const __grid_cons
           const float2 f = ffma2(Cq[p], dy2, fa[p]);
           const float2 w = fmul2(f, q);
           dA[p] = ffma2(dt2, w, dA[p]);
-          sAw = ffma2(An[p], w, sAw);
+          sAw = ffma2(An_at(p), w, sAw);
           sBf = ffma2(Bq[p], f, sBf);
           vb[p] = fmul2(dx2, f);
           fa[p] = fmul2(f, al);
