@@ -147,6 +147,16 @@ __device__ __forceinline__ float softplus_f(float x) {
   const float r = x < -3.f ? series : lg2(1.f + e) * kLn2;
   return x > 20.f ? x : r;
 }
+// softplus(x) and its derivative sigmoid(x) = e / (1 + e), e = e^x, from one
+// exponential (same forms and ranges as softplus_f).
+__device__ __forceinline__ float softplus_sig(float x, float& sig) {
+  const float e = ex2(fminf(x, 20.f) * kLog2e);
+  sig = x > 20.f ? 1.f : e * rcp(1.f + e);
+  const float p = 0.2f - e * (1.f / 6.f);
+  const float series = e * (1.f - e * (0.5f - e * (1.f / 3.f - e * (0.25f - e * p))));
+  const float r = x < -3.f ? series : lg2(1.f + e) * kLn2;
+  return x > 20.f ? x : r;
+}
 // logistic sigmoid
 __device__ __forceinline__ float sigmoid_f(float x) { return rcp(1.f + ex2(-x * kLog2e)); }
 

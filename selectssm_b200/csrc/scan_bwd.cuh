@@ -258,15 +258,16 @@ __global__ void __launch_bounds__(kBThreads, 2) ssm_bwd_kernel(const __grid_cons
       // ---- per-step scalars of the block (own channel)
       // (sgv: upstream gradient of the skip term in the scan frame; it differs
       // from dyv only for the reference's reverse-skip frame)
-      // (zgv: act'(z) of the step, for dz)
-      float dtv[kCk], dxv[kCk], dyv[kCk], sgv[kCk], zgv[kCk];
+      // (zgv: act'(z) of the step, for dz; spv: d softplus / d delta, for ddelta)
+      float dtv[kCk], dxv[kCk], dyv[kCk], sgv[kCk], zgv[kCk], spv[kCk];
 #pragma unroll
       for (int u = 0; u < kCk; ++u) {
         const int tl = T0 + u;
         const bool valid = j * kChunk + tl < L;
         const float x = ld_f(su + tl * kBTile);
         const float dr = ld_f(sd + tl * kBTile) + bias;
-        const float dt = softplus ? softplus_f(dr) : dr;
+        spv[u] = 1.f;
+        const float dt = softplus ? softplus_sig(dr, spv[u]) : dr;
         dtv[u] = valid ? dt : 0.f;
         dxv[u] = valid ? dt * x : 0.f;
         const int row = rev ? kChunk - 1 - tl : tl;
@@ -373,8 +374,7 @@ __global__ void __launch_bounds__(kBThreads, 2) ssm_bwd_kernel(const __grid_cons
         const float du = fmaf(Dsc, sgv[u], dtv[u] * sbf);  // Dsc is 0 without a skip
         dD_acc = fmaf(sgv[u], x, dD_acc);
         float g = fmaf(x, sbf, saw);  // d/d dt
-        const float sig = sigmoid_f(ld_f(sd + tl * kBTile) + bias);
-        g *= softplus ? sig : 1.f;
+        g *= spv[u];
         db_acc += g;
         if (t < L && cvalid) {
           st_act(du_g + (size_t)t * Dm, du);
