@@ -219,7 +219,7 @@ constexpr int kSMs = 148;
 // The forward's CTAs are small and latency bound, so its "waves" are effective
 // sizes fitted to measurements (batch 8 runs best unsegmented with 384 CTAs,
 // batch 2 with 16 segments) rather than occupancy limits.
-constexpr SegPolicy kFwdSeg{kTileCh, 384, 768, 0.55};
+constexpr SegPolicy kFwdSeg{kTileCh, 384, 1536, 0.55};
 constexpr SegPolicy kBwdSeg{kBTile, 2L * kSMs, 4L * kSMs, 0.5};
 
 static Seg choose_segments(const Geo& g, SegPolicy pol) {
