@@ -168,31 +168,73 @@ def cpu_reference_step(inp, chunk_size=None):
     return out, du, ddelta, dz, dA, dB, dC, dD
 
 
-def cpu_threads():
+def cpu_cores():
     try:
-        from threadpoolctl import threadpool_info
-        n = [i.get("num_threads", 1) for i in threadpool_info()]
-        return max(n) if n else 1
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+_SAMPLE_INP = {}
+
+
+def _one_thread():
+    try:
+        from threadpoolctl import threadpool_limits
+        threadpool_limits(1)
     except Exception:
-        return 1
+        pass
 
 
-def run_cpu_sample(seqlen=4096, reps=1, warm_seqlen=256):
-    """Oracle fwd+bwd on one batch row of the workload (the full sequence by
-    default: about 5-15 s of CPU work), after a short warm-up."""
-    B, D, N = 1, CFG["dim"], CFG["dstate"]
-    cpu_reference_step(host_inputs(1, B, warm_seqlen, D, N))  # warm
-    inp = host_inputs(0, B, seqlen, D, N)
-    t0 = time.perf_counter()
-    for _ in range(reps):
-        cpu_reference_step(inp)
-    dt = (time.perf_counter() - t0) / reps
-    units = B * seqlen * D
-    sample = (f"NumPy restatement of the reference algorithm (chunked scan fwd + custom-VJP bwd, "
-              f"float32) on one batch row of the config-2 workload: batch=1, L={seqlen}, d_inner={D}, N={N}; "
-              f"{reps} rep(s) after a warm-up at L={warm_seqlen}; elementwise work single-threaded, "
-              f"BLAS threads {cpu_threads()}")
-    return units / dt, dt, sample
+def _run_shard(span):
+    """Oracle fwd+bwd on channels [s, e) of the shared sample (B and C are
+    shared by all channels; each channel's scan is independent)."""
+    s, e = span
+    inp = _SAMPLE_INP
+    sub = {k: (v[..., s:e] if k in ("u", "delta", "z", "dout") else v[s:e] if k in ("A", "D") else v)
+           for k, v in inp.items()}
+    cpu_reference_step(sub)
+    return e - s
+
+
+class CpuSampler:
+    """Times the NumPy restatement of the reference algorithm on all host
+    cores: the channels of one fixed sample are split over one single-threaded
+    process per core (the reference's JAX-on-CPU would also use every core).
+    The workers are forked after the sample is drawn, so they share it."""
+
+    def __init__(self, seqlen, batch=1):
+        import multiprocessing as mp
+        global _SAMPLE_INP
+        D, N = CFG["dim"], CFG["dstate"]
+        _SAMPLE_INP = host_inputs(0, batch, seqlen, D, N)
+        self.procs = cpu_cores()
+        k = self.procs
+        self.spans = [(D * i // k, D * (i + 1) // k) for i in range(k)]
+        self.units = batch * seqlen * D
+        self.sample = (f"NumPy restatement of the reference algorithm (chunked scan fwd + custom-VJP bwd, float32) "
+                       f"on batch={batch}, L={seqlen}, d_inner={D}, N={N} of the config-2 workload, channels split "
+                       f"over {k} single-threaded processes (one per host core), after one warm-up run")
+        self.pool = mp.get_context("fork").Pool(k, initializer=_one_thread)
+        self.pool.map(_run_shard, self.spans)  # warm-up (imports, page faults)
+
+    def run(self):
+        t0 = time.perf_counter()
+        self.pool.map(_run_shard, self.spans)
+        dt = time.perf_counter() - t0
+        return self.units / dt, dt, self.sample
+
+    def close(self):
+        self.pool.close()
+        self.pool.join()
+
+
+def run_cpu_sample(seqlen=4096, batch=1):
+    sampler = CpuSampler(seqlen, batch)
+    try:
+        return sampler.run()
+    finally:
+        sampler.close()
 
 
 # ----------------------------------------------------------------------------- GPU arm
@@ -228,21 +270,23 @@ def main():
             return
         steps = max(1, args.steps)
         vals = []
-        # each step times the oracle on one batch row of L=64 (about 0.1 s on the
-        # host cores), so the default 1000 steps finish within about two minutes
+        # each step times the oracle on one full-width batch row of L=256, split
+        # over all host cores (about 0.1 s), so 1000 steps stay within minutes
+        sampler = CpuSampler(256)
         for _ in range(args.warmup):
-            run_cpu_sample(seqlen=64, warm_seqlen=16)
+            sampler.run()
         t0 = time.perf_counter()
         for _ in range(steps):
-            v, _, sample = run_cpu_sample(seqlen=64, warm_seqlen=16)
+            v, _, sample = sampler.run()
             vals.append(v)
+        sampler.close()
         total = time.perf_counter() - t0
         v = statistics.median(vals)
         line = {"metric": METRIC, "value": v, "unit": UNIT, "n_gpus": world, "steps": steps,
                 "warmup": args.warmup, "ms_per_step": 1e3 * total / steps, "higher_is_better": True,
                 "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": config,
                 "impl": "reference",
-                "cpu_baseline": {"value": v, "unit": UNIT, "cores": cpu_threads(), "kind": "port",
+                "cpu_baseline": {"value": v, "unit": UNIT, "cores": cpu_cores(), "kind": "port",
                                  "sample": sample},
                 "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
         print(json.dumps(line))
@@ -421,8 +465,8 @@ def main():
             "gpu_launches": n_launches,
             "clocks": clk.summary(), "library": lib.ssm_version().decode()}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        v, secs, sample = run_cpu_sample()
-        line["cpu_baseline"] = {"value": v, "unit": UNIT, "cores": cpu_threads(), "kind": "port",
+        v, secs, sample = run_cpu_sample(batch=2)  # about 1 s on 16 cores: ~16 core-seconds of work
+        line["cpu_baseline"] = {"value": v, "unit": UNIT, "cores": cpu_cores(), "kind": "port",
                                 "sample": sample, "seconds": secs}
     if rank == 0:
         print(json.dumps(line))
