@@ -46,8 +46,8 @@ struct FwdSmem {
   static constexpr int kOffU = 0, kOffDelta = kAct, kOffZ = 2 * kAct, kOffUo = 3 * kAct;
   static constexpr int kOffB = 4 * kAct, kOffC = 4 * kAct + kBC;
   static constexpr int kStage = 4 * kAct + 2 * kBC;
-  static constexpr int kBars = kStage * kFStages;
-  static constexpr int kBytes = kBars + 8 * kFStages;
+  static constexpr int kBars = kStage * kFStages;  // full[kFStages] then empty[kFStages]
+  static constexpr int kBytes = kBars + 16 * kFStages;
 };
 
 
@@ -83,7 +83,10 @@ __global__ void __launch_bounds__(kFThreads, 6) ssm_fwd_kernel(const __grid_cons
   const int oc0 = comp ? Dm - kTileCh - c0 : c0;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kFStages; ++s) mbar_init(&bars[s], 1);
+    for (int s = 0; s < kFStages; ++s) {
+      mbar_init(&bars[s], 1);                            // full: the TMA loads of the stage landed
+      mbar_init(&bars[kFStages + s], kFThreads / 32);    // empty: every warp is done with the stage
+    }
     fence_mbar_init();
   }
   __syncthreads();
@@ -138,8 +141,8 @@ __global__ void __launch_bounds__(kFThreads, 6) ssm_fwd_kernel(const __grid_cons
     const int jl = j - j0;
     const int s = jl % kFStages;
     const bool ok = mbar_wait_bounded(&bars[s], (jl / kFStages) & 1);
-    if (!__syncthreads_and(ok)) {
-      if (threadIdx.x == 0) report(a.status, kStatusTimeout);
+    if (!__all_sync(kFull, ok)) {  // warps proceed independently; a stalled load ends this warp
+      if (lane == 0) report(a.status, kStatusTimeout);
       return;
     }
     const unsigned char* st = smem + s * S::kStage;
@@ -228,8 +231,13 @@ __global__ void __launch_bounds__(kFThreads, 6) ssm_fwd_kernel(const __grid_cons
         default: epilogue(std::integral_constant<int, SSM_ACT_NONE>{}); break;
       }
     }
-    __syncthreads();
-    if (threadIdx.x == 0 && jl + kFStages < nloc) {
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&bars[kFStages + s]);  // this warp no longer reads stage s
+    if (threadIdx.x == 0 && jl + kFStages < nloc) {  // refill stage s once every warp released it
+      if (!mbar_wait_bounded(&bars[kFStages + s], (jl / kFStages) & 1)) {
+        report(a.status, kStatusTimeout);
+        return;
+      }
       fence_proxy_async_smem();
       issue(jl + kFStages);
     }
