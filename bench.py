@@ -237,6 +237,110 @@ def run_cpu_sample(seqlen=4096, batch=1):
         sampler.close()
 
 
+# ----------------------------------------------------------------------------- other workloads
+OTHER = {
+    3: dict(workload="config 3: BidirectionalMamba scan pair, complement + tied gate + concat, bf16 I/O, "
+                     "fp32 state", batch=2, seqlen=131072, dim=512, dtype="bf16", bidir=True),
+    4: dict(workload="config 4: long-sequence raw op fwd+bwd (recursive-scan semantics), fp32",
+            batch=1, seqlen=1 << 20, dim=1024, dtype="f32", bidir=False),
+    5: dict(workload="config 5: raw op fwd+bwd, bf16 I/O, fp32 state", batch=64, seqlen=2048, dim=1536,
+            dtype="bf16", bidir=False),
+}
+
+
+def run_other_config(args):
+    """Device-resident fwd+bwd timing of configs 3-5 (seeded on the device with
+    the configs' distributions), with the same event, warm-up and clock rules as
+    the config-2 line.  Algorithmic bytes per unit: 11 s + 6 s N / D, where a
+    unit is one (b, l, d) per direction; config 3's tied z is read once for
+    both directions, so 9.5 s + 6 s N / D there."""
+    import torch
+    import selectssm_b200 as S
+    from selectssm_b200 import _lib
+
+    c = OTHER[args.config]
+    Bsz, L, D, N = c["batch"], c["seqlen"], c["dim"], 16
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    lib = _lib.load()
+    dt = torch.bfloat16 if c["dtype"] == "bf16" else torch.float32
+    g = torch.Generator(device=dev).manual_seed(args.config)
+
+    def draw():
+        n = lambda *s: torch.randn(*s, generator=g, device=dev)  # noqa: E731
+        t = {"u": n(Bsz, L, D).to(dt), "delta": (n(Bsz, L, D) - 4.0).to(dt), "B": n(Bsz, L, N).to(dt),
+             "C": n(Bsz, L, N).to(dt), "A": -(1.0 + 15.0 * torch.rand(D, N, generator=g, device=dev)),
+             "D": 1.0 + 0.1 * n(D), "bias": 0.1 * n(D)}
+        return {k: v.requires_grad_() for k, v in t.items()}
+
+    dirs = 2 if c["bidir"] else 1
+    fwd_in = draw()
+    rev_in = draw() if c["bidir"] else None
+    z = torch.randn(Bsz, L, D, generator=g, device=dev).to(dt).requires_grad_()
+    dout = torch.randn(Bsz, L, dirs * D, generator=g, device=dev).to(dt)
+    names = ("u", "delta", "A", "B", "C", "D", "bias")
+
+    def step(marks=None):
+        for t in (fwd_in, rev_in, {"z": z}):
+            for v in (t or {}).values():
+                v.grad = None
+        if marks:
+            marks[0].record()
+        if c["bidir"]:
+            out = S.selective_scan_bidir(*(fwd_in[k] for k in names), z, *(rev_in[k] for k in names), z,
+                                         complement=True)
+        else:
+            f = fwd_in
+            out = S.selective_scan(f["u"], f["delta"], f["A"], f["B"], f["C"], D=f["D"], z=z,
+                                   delta_bias=f["bias"], delta_softplus=True)
+        if marks:
+            marks[1].record()
+        out.backward(dout)
+        if marks:
+            marks[2].record()
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(0) as clk:
+        clk.wait_first()
+        n0 = lib.ssm_launch_count()
+        e0.record(stream)
+        for _ in range(args.steps):
+            step()
+        e1.record(stream)
+        n_launches = lib.ssm_launch_count() - n0
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    split = []  # per-call forward / backward times, calls queued back to back
+    for _ in range(5):
+        m = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+        step(m)
+        split.append(m)
+    torch.cuda.synchronize()
+    t_fwd = statistics.median(m[0].elapsed_time(m[1]) for m in split[1:])
+    t_bwd = statistics.median(m[1].elapsed_time(m[2]) for m in split[1:])
+    units = Bsz * L * D * dirs
+    s = 2 if dt == torch.bfloat16 else 4
+    per_unit = (9.5 if c["bidir"] else 11.0) * s + 6 * s * N / D
+    hbm, src = peaks()
+    achieved = units * per_unit / (ms * 1e-3) / 1e9
+    line = {"metric": METRIC, "value": units / (ms * 1e-3), "unit": UNIT, "n_gpus": 1, "steps": args.steps,
+            "warmup": max(3, args.warmup), "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": c["dtype"], "data": "synthetic",
+            "config": {"workload": c["workload"], "batch_per_gpu": Bsz, "seq_len": L, "d_inner": D, "d_state": N,
+                       "directions": dirs, "parallelism": "single GPU",
+                       "l2": "inputs larger than L2, no flush"},
+            "roofline_step": {"bound": "hbm", "achieved": achieved, "peak": hbm, "peak_source": src, "unit": "GB/s",
+                              "frac": achieved / hbm, "bytes_per_unit": per_unit},
+            "ms_fwd_call": t_fwd, "ms_bwd_call": t_bwd,
+            "e2e": None, "gpu_launches": n_launches, "clocks": clk.summary(),
+            "library": lib.ssm_version().decode()}
+    print(json.dumps(line))
+
+
 # ----------------------------------------------------------------------------- GPU arm
 def main():
     ap = argparse.ArgumentParser()
@@ -247,6 +351,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=20)
     ap.add_argument("--batch", type=int, default=None, help="override batch per GPU (small profiling cases)")
+    ap.add_argument("--config", type=int, default=2, choices=[2, 3, 4, 5],
+                    help="2 (default) is the benchmark line; 3, 4 and 5 time the other contract workloads "
+                         "device-resident on one GPU (no e2e or CPU legs)")
     ap.add_argument("--parallel", default="batch", choices=["batch", "channels"],
                     help="N>1 sharding: batch rows (default) or d_inner channels with B/C replicated")
     args = ap.parse_args()
@@ -254,6 +361,10 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.config != 2:
+        if world != 1 or args.impl != "ours":
+            raise SystemExit("--config 3/4/5 time one GPU with the CUDA path only")
+        return run_other_config(args)
     if args.batch:
         CFG["batch"] = args.batch
     Bsz, L, D, N = CFG["batch"], CFG["seqlen"], CFG["dim"], CFG["dstate"]

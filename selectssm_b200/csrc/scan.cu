@@ -52,6 +52,33 @@ __global__ void zero_rows16_kernel(float* p, int64_t rows, int64_t stride) {
   reinterpret_cast<float4*>(p + r * stride)[i & 3] = make_float4(0.f, 0.f, 0.f, 0.f);
 }
 
+// Widens the bf16 rows of B and C (16 elements, row stride `stride` elements)
+// to dense float32 rows, one 16-byte load (8 elements) per thread and tensor.
+// The scan kernels read every B / C element once per channel, so converting
+// once per call here is cheaper than converting in every lane.
+__global__ void widen_bc_kernel(const __nv_bfloat16* __restrict__ Bm, const __nv_bfloat16* __restrict__ Cm,
+                                int64_t rows, int64_t stride, float* __restrict__ Bw, float* __restrict__ Cw) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= rows * 2) return;
+  const int64_t r = i >> 1, h = (i & 1) * 8;
+  const __nv_bfloat16* src[2] = {Bm, Cm};
+  float* dst[2] = {Bw, Cw};
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {
+    const uint4 v = *reinterpret_cast<const uint4*>(src[k] + r * stride + h);
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+    float f[8];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      f[2 * j] = __uint_as_float(w[j] << 16);
+      f[2 * j + 1] = __uint_as_float(w[j] & 0xffff0000u);
+    }
+    float4* o = reinterpret_cast<float4*>(dst[k] + r * kN + h);
+    o[0] = make_float4(f[0], f[1], f[2], f[3]);
+    o[1] = make_float4(f[4], f[5], f[6], f[7]);
+  }
+}
+
 template <typename TBC>
 __global__ void finalize_kernel(FinalizeDir f) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -247,20 +274,27 @@ static Seg choose_segments(const Geo& g, SegPolicy pol) {
   return pick;
 }
 
-static size_t fwd_ws_bytes(const Geo& g) {
+// float32 copies of bf16 B and C rows (see widen_bc_kernel)
+static size_t wide_bc_bytes(const Geo& g) {
+  return g.bcbf16 ? 2 * round256((size_t)g.B * g.L * kN * 4) : 0;
+}
+
+static size_t fwd_seg_bytes(const Geo& g) {
   const Seg sg = choose_segments(g, kFwdSeg);
   if (sg.nseg <= 1) return 0;
   const size_t rows = (size_t)g.B * sg.nseg * g.Dm;
   return round256(rows * kN * 4) + round256(rows * 4);
 }
 
+static size_t fwd_ws_bytes(const Geo& g) { return fwd_seg_bytes(g) + wide_bc_bytes(g); }
+
 static size_t bwd_ws_bytes(const Geo& g) {
   const Seg sg = choose_segments(g, kBwdSeg);
   const size_t rows = (size_t)g.B * sg.nseg * g.Dm;
   size_t n = round256(rows * kN * 4) + 2 * round256(rows * 4);
-  if (g.bcbf16) n += 2 * round256((size_t)g.B * g.L * kN * 4);
+  if (g.bcbf16) n += 2 * round256((size_t)g.B * g.L * kN * 4);  // float32 dB / dC accumulators
   if (sg.nseg > 1) n += round256(rows * kN * 4) + round256(rows * 4);  // segF, segT
-  return n;
+  return n + wide_bc_bytes(g);
 }
 
 static size_t ws_bytes(const Geo& g) {
@@ -268,14 +302,44 @@ static size_t ws_bytes(const Geo& g) {
   return a > b ? a : b;
 }
 
+static int launch_widen_bc(const ssm_params_t* p, const Geo& g, float* Bw, float* Cw, cudaStream_t s) {
+  const int64_t rows = (int64_t)g.B * g.L;
+  const int threads = 256;
+  const unsigned blocks = (unsigned)((rows * 2 + threads - 1) / threads);
+  widen_bc_kernel<<<blocks, threads, 0, s>>>(static_cast<const __nv_bfloat16*>(p->Bm),
+                                              static_cast<const __nv_bfloat16*>(p->Cm), rows, g.bs, Bw, Cw);
+  note_launches(1);
+  SSM_CUDA_CHECK(cudaGetLastError(), "launch widen_bc_kernel");
+  return SSM_OK;
+}
+
+// B / C maps: the caller's rows, or the widened float32 copy when B / C are bf16
+static bool make_bc_maps(const ssm_params_t* p, const Geo& g, const float* Bw, const float* Cw, CUtensorMap* tB,
+                         CUtensorMap* tC) {
+  if (g.bcbf16) {
+    const uint64_t rs = kN * 4;
+    return make_map(tB, Bw, false, kN, g.L, g.B, rs, (uint64_t)g.L * rs, kN, kChunk) &&
+           make_map(tC, Cw, false, kN, g.L, g.B, rs, (uint64_t)g.L * rs, kN, kChunk);
+  }
+  const uint64_t rs = g.bs * 4;
+  return make_map(tB, p->Bm, false, kN, g.L, g.B, rs, (uint64_t)g.L * rs, kN, kChunk) &&
+         make_map(tC, p->Cm, false, kN, g.L, g.B, rs, (uint64_t)g.L * rs, kN, kChunk);
+}
+
 // ---------------------------------------------------------------- forward launch
-static int fill_fwd_dir(const ssm_params_t* p, const Geo& g, FwdDir* d) {
-  const uint64_t es = g.es, eb = g.esbc;
+static int fill_fwd_dir(const ssm_params_t* p, const Geo& g, FwdDir* d, cudaStream_t s) {
+  const uint64_t es = g.es;
+  char* ws = static_cast<char*>(p->workspace);
+  float* Bw = g.bcbf16 ? reinterpret_cast<float*>(ws + fwd_seg_bytes(g)) : nullptr;
+  float* Cw = g.bcbf16 ? reinterpret_cast<float*>(ws + fwd_seg_bytes(g) + wide_bc_bytes(g) / 2) : nullptr;
+  if (g.bcbf16) {
+    const int st = launch_widen_bc(p, g, Bw, Cw, s);
+    if (st) return st;
+  }
   bool ok = make_map(&d->tm_u, p->u, g.bf16, g.Dm, g.L, g.B, g.Dm * es, (uint64_t)g.L * g.Dm * es, kTileCh, kChunk);
   ok = ok && make_map(&d->tm_delta, p->delta, g.bf16, g.Dm, g.L, g.B, g.Dm * es, (uint64_t)g.L * g.Dm * es,
                       kTileCh, kChunk);
-  ok = ok && make_map(&d->tm_B, p->Bm, g.bcbf16, kN, g.L, g.B, g.bs * eb, (uint64_t)g.L * g.bs * eb, kN, kChunk);
-  ok = ok && make_map(&d->tm_C, p->Cm, g.bcbf16, kN, g.L, g.B, g.bs * eb, (uint64_t)g.L * g.bs * eb, kN, kChunk);
+  ok = ok && make_bc_maps(p, g, Bw, Cw, &d->tm_B, &d->tm_C);
   if (p->z)
     ok = ok && make_map(&d->tm_z, p->z, g.bf16, g.Dm, g.L, g.B, g.zs * es, (uint64_t)g.L * g.zs * es, kTileCh,
                         kChunk);
@@ -331,16 +395,15 @@ static int launch_fwd_t(FwdLaunch& L, int ndir, const Geo& g, cudaStream_t s) {
   return SSM_OK;
 }
 
+// B / C always reach the kernels as float32 (bf16 rows are widened first)
 static int launch_fwd(FwdLaunch& L, int ndir, const Geo& g, cudaStream_t s) {
-  if (!g.bf16 && !g.bcbf16) return launch_fwd_t<float, float>(L, ndir, g, s);
-  if (!g.bf16 && g.bcbf16) return launch_fwd_t<float, __nv_bfloat16>(L, ndir, g, s);
-  if (g.bf16 && !g.bcbf16) return launch_fwd_t<__nv_bfloat16, float>(L, ndir, g, s);
-  return launch_fwd_t<__nv_bfloat16, __nv_bfloat16>(L, ndir, g, s);
+  if (g.bf16) return launch_fwd_t<__nv_bfloat16, float>(L, ndir, g, s);
+  return launch_fwd_t<float, float>(L, ndir, g, s);
 }
 
 // ---------------------------------------------------------------- backward launch
 struct BwdWs {
-  float *dA_part, *dD_part, *db_part, *dB_acc, *dC_acc, *segF, *segT;
+  float *dA_part, *dD_part, *db_part, *dB_acc, *dC_acc, *segF, *segT, *Bw, *Cw;
   int64_t acc_stride;
 };
 
@@ -364,21 +427,28 @@ static void carve_ws(const ssm_params_t* p, const Geo& g, char* ws, BwdWs* w) {
     w->dB_acc = reinterpret_cast<float*>(ws);
     ws += round256((size_t)g.B * g.L * kN * 4);
     w->dC_acc = reinterpret_cast<float*>(ws);
+    ws += round256((size_t)g.B * g.L * kN * 4);
     w->acc_stride = kN;
+    w->Bw = reinterpret_cast<float*>(ws);
+    w->Cw = reinterpret_cast<float*>(ws + wide_bc_bytes(g) / 2);
   } else {
+    w->Bw = w->Cw = nullptr;
     w->dB_acc = reinterpret_cast<float*>(p->dB);
     w->dC_acc = reinterpret_cast<float*>(p->dC);
     w->acc_stride = g.bs;
   }
 }
 
-static int fill_bwd_dir(const ssm_params_t* p, const Geo& g, const BwdWs& w, BwdDir* d) {
-  const uint64_t es = g.es, eb = g.esbc;
+static int fill_bwd_dir(const ssm_params_t* p, const Geo& g, const BwdWs& w, BwdDir* d, cudaStream_t s) {
+  const uint64_t es = g.es;
+  if (g.bcbf16) {
+    const int st = launch_widen_bc(p, g, w.Bw, w.Cw, s);
+    if (st) return st;
+  }
   bool ok = make_map(&d->tm_u, p->u, g.bf16, g.Dm, g.L, g.B, g.Dm * es, (uint64_t)g.L * g.Dm * es, kBTile, kChunk);
   ok = ok && make_map(&d->tm_delta, p->delta, g.bf16, g.Dm, g.L, g.B, g.Dm * es, (uint64_t)g.L * g.Dm * es,
                       kBTile, kChunk);
-  ok = ok && make_map(&d->tm_B, p->Bm, g.bcbf16, kN, g.L, g.B, g.bs * eb, (uint64_t)g.L * g.bs * eb, kN, kChunk);
-  ok = ok && make_map(&d->tm_C, p->Cm, g.bcbf16, kN, g.L, g.B, g.bs * eb, (uint64_t)g.L * g.bs * eb, kN, kChunk);
+  ok = ok && make_bc_maps(p, g, w.Bw, w.Cw, &d->tm_B, &d->tm_C);
   ok = ok && make_map(&d->tm_dout, p->dout, g.bf16, g.Dm, g.L, g.B, g.os * es, (uint64_t)g.L * g.os * es, kBTile,
                       kChunk);
   if (p->z)
@@ -473,10 +543,8 @@ static int launch_bwd(BwdLaunch& L, int ndir, const Geo& g, cudaStream_t s) {
     const int st = launch_bwd(L, 1, g, s);
     return st ? st : launch_bwd(L1, 1, g, s);
   }
-  if (!g.bf16 && !g.bcbf16) return launch_bwd_g<float, float>(L, ndir, g, s);
-  if (!g.bf16 && g.bcbf16) return launch_bwd_g<float, __nv_bfloat16>(L, ndir, g, s);
-  if (g.bf16 && !g.bcbf16) return launch_bwd_g<__nv_bfloat16, float>(L, ndir, g, s);
-  return launch_bwd_g<__nv_bfloat16, __nv_bfloat16>(L, ndir, g, s);
+  if (g.bf16) return launch_bwd_g<__nv_bfloat16, float>(L, ndir, g, s);  // B / C widened to float32
+  return launch_bwd_g<float, float>(L, ndir, g, s);
 }
 
 static int launch_zero_acc(const Geo& g, const BwdWs& w, cudaStream_t s) {
@@ -567,10 +635,11 @@ int ssm_fwd_bidir(const ssm_params_t* fwd, const ssm_params_t* rev, ssm_stream_t
   }
   FwdLaunch args;
   std::memset(&args, 0, sizeof(args));
-  st = fill_fwd_dir(fwd, g, &args.dir[0]);
-  if (!st && rev) st = fill_fwd_dir(rev, g, &args.dir[1]);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  st = fill_fwd_dir(fwd, g, &args.dir[0], s);
+  if (!st && rev) st = fill_fwd_dir(rev, g, &args.dir[1], s);
   if (st) return st;
-  return launch_fwd(args, rev ? 2 : 1, g, reinterpret_cast<cudaStream_t>(stream));
+  return launch_fwd(args, rev ? 2 : 1, g, s);
 }
 
 int ssm_bwd(const ssm_params_t* p, ssm_stream_t stream) { return ssm_bwd_bidir(p, nullptr, stream); }
@@ -609,7 +678,7 @@ int ssm_bwd_bidir(const ssm_params_t* fwd, const ssm_params_t* rev, ssm_stream_t
   BwdLaunch args;
   std::memset(&args, 0, sizeof(args));
   for (int d = 0; d < ndir; ++d) {
-    st = fill_bwd_dir(ps[d], g, w[d], &args.dir[d]);
+    st = fill_bwd_dir(ps[d], g, w[d], &args.dir[d], s);
     if (st) return st;
     st = launch_zero_acc(g, w[d], s);
     if (st) return st;
