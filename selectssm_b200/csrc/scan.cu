@@ -1,5 +1,6 @@
 // C-ABI entry points for the selective scan (forward, backward, bidirectional),
 // their argument checks, TMA descriptor set-up and launch sequences.
+#include <algorithm>
 #include <cstdio>
 #include <cstring>
 #include <atomic>
@@ -160,6 +161,7 @@ struct Geo {
   int es, esbc;  // element sizes
   bool bf16, bcbf16;
   int64_t zs, os, bs;  // row strides in elements
+  int ndir;             // directions in one launch (2 for the *_bidir calls)
 };
 
 static int check_common(const ssm_params_t* p, Geo* g) {
@@ -170,6 +172,7 @@ static int check_common(const ssm_params_t* p, Geo* g) {
   if ((p->dtype != SSM_F32 && p->dtype != SSM_BF16) || (p->bc_dtype != SSM_F32 && p->bc_dtype != SSM_BF16))
     return SSM_ERR_DTYPE;
   if (p->gate_act < SSM_ACT_NONE || p->gate_act > SSM_ACT_RELU) return SSM_ERR_SHAPE;
+  g->ndir = 1;
   g->B = p->batch;
   g->L = p->seqlen;
   g->Dm = p->dim;
@@ -237,6 +240,8 @@ struct Seg {
   int nseg, seg_chunks;
 };
 struct SegPolicy {
+  int max_seg;      // segment cap
+  bool per_launch;  // count the chains of both directions of a bidirectional launch
   int tile;         // channels per CTA
   long slots;       // resident CTAs of the main kernel on the GPU
   long agg_slots;   // resident CTAs of the pre-pass
@@ -246,17 +251,22 @@ constexpr int kSMs = 148;
 // The forward's CTAs are small and latency bound, so its "waves" are effective
 // sizes fitted to measurements (batch 8 runs best unsegmented with 384 CTAs,
 // batch 2 with 16 segments) rather than occupancy limits.
-constexpr SegPolicy kFwdSeg{kTileCh, 384, 1536, 0.55};
-constexpr SegPolicy kBwdSeg{kBTile, 2L * kSMs, 4L * kSMs, 0.5};
+// Its cap is lower because each segment folds the end states of all segments
+// before it (quadratic in the segment count).  Its fitted sizes hold per
+// direction: a bidirectional launch (B=2, L=131072, 512 channels) ran faster with the
+// per-direction choice than with one that counts both directions' chains.
+constexpr SegPolicy kFwdSeg{64, false, kTileCh, 384, 1536, 0.55};
+constexpr SegPolicy kBwdSeg{256, true, kBTile, 2L * kSMs, 4L * kSMs, 0.5};
 
 static Seg choose_segments(const Geo& g, SegPolicy pol) {
   const int nblk = (g.L + kChunk - 1) / kChunk;
   if (nblk == 0) return {1, 1};
-  const long chains = (long)((g.Dm + pol.tile - 1) / pol.tile) * g.B;
+  // both directions of a bidirectional call share the launch
+  const long chains = (long)((g.Dm + pol.tile - 1) / pol.tile) * g.B * (pol.per_launch ? g.ndir : 1);
   if (chains <= 0) return {1, nblk};
   int max_seg = nblk / 4;  // at least 4 stages (64 steps) per segment
   if (max_seg < 1) max_seg = 1;
-  if (max_seg > 64) max_seg = 64;
+  if (max_seg > pol.max_seg) max_seg = pol.max_seg;
   double best = 0.0;
   Seg pick{1, nblk};
   for (int n = 1; n <= max_seg; ++n) {
@@ -297,9 +307,16 @@ static size_t bwd_ws_bytes(const Geo& g) {
   return n + wide_bc_bytes(g);
 }
 
+// The segment count depends on whether the call is bidirectional, which a
+// single parameter set does not say: size for both.
 static size_t ws_bytes(const Geo& g) {
-  const size_t a = fwd_ws_bytes(g), b = bwd_ws_bytes(g);
-  return a > b ? a : b;
+  size_t n = 0;
+  for (int nd = 1; nd <= 2; ++nd) {
+    Geo h = g;
+    h.ndir = nd;
+    n = std::max({n, fwd_ws_bytes(h), bwd_ws_bytes(h)});
+  }
+  return n;
 }
 
 static int launch_widen_bc(const ssm_params_t* p, const Geo& g, float* Bw, float* Cw, cudaStream_t s) {
@@ -623,6 +640,7 @@ int ssm_fwd_bidir(const ssm_params_t* fwd, const ssm_params_t* rev, ssm_stream_t
     st = check_fwd(rev, &g2);
     if (st) return st;
     if (!same_geo(g, g2)) return SSM_ERR_SHAPE;
+    g.ndir = 2;
   }
   if ((int64_t)g.B * g.L * g.Dm == 0) return SSM_OK;
   st = bind_device(fwd->u);
@@ -652,6 +670,7 @@ int ssm_bwd_bidir(const ssm_params_t* fwd, const ssm_params_t* rev, ssm_stream_t
     st = check_bwd(rev, &g2);
     if (st) return st;
     if (!same_geo(g, g2)) return SSM_ERR_SHAPE;
+    g.ndir = 2;
   }
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   st = bind_device((int64_t)g.B * g.L * g.Dm ? fwd->u : (const void*)fwd->dA);
