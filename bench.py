@@ -356,6 +356,9 @@ def main():
                          "device-resident on one GPU (no e2e or CPU legs)")
     ap.add_argument("--parallel", default="batch", choices=["batch", "channels"],
                     help="N>1 sharding: batch rows (default) or d_inner channels with B/C replicated")
+    ap.add_argument("--bc-sum", default="multicast", choices=["multicast", "nccl"],
+                    help="channel sharding: sum dB/dC inside the backward kernel over NVLink multicast "
+                         "(default, when the GPUs support it) or with an NCCL all-reduce after it")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -372,8 +375,7 @@ def main():
               "batch_per_gpu": Bsz, "global_batch": Bsz * world, "seq_len": L, "d_inner": D, "d_state": N,
               "parallelism": ("single GPU" if world == 1 else
                               f"batch-sharded dp{world}, NCCL all-reduce of dA/dD in bwd" if args.parallel == "batch"
-                              else f"d_inner-sharded x{world} ({D} channels per GPU), B/C replicated, "
-                                   "NCCL all-reduce of dB/dC in bwd"),
+                              else f"d_inner-sharded x{world} ({D} channels per GPU), B/C replicated, dB/dC"),
               "l2": "inputs larger than L2 (u, dt, z, dy = 805 MB per step), no flush"}
 
     if args.impl == "reference":
@@ -407,7 +409,7 @@ def main():
     import torch.distributed as dist
     import selectssm_b200 as S
     from selectssm_b200 import _lib
-    from selectssm_b200.parallel import allreduce_grads, replicated_bc
+    from selectssm_b200.parallel import MulticastBCSum, allreduce_grads, replicated_bc
 
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
@@ -422,15 +424,23 @@ def main():
         t[k].requires_grad_(True)
 
     pending = []
+    bcs = None
+    if chan and args.bc_sum == "multicast":
+        bcs = MulticastBCSum(Bsz, L, device=dev)
+        if not bcs.available:
+            bcs = None
+    if chan:
+        config["parallelism"] += (" summed inside the backward kernel by NVLink multicast (multimem.red)" if bcs
+                                  else " summed by an NCCL all-reduce after the backward")
 
     def step(inputs):
         for k in ("u", "delta", "z", "A", "B", "C", "D"):
             inputs[k].grad = None
         Bm, Cm = inputs["B"], inputs["C"]
-        if chan:  # channel sharding: the B / C gradients are summed over ranks in the backward
+        if chan and bcs is None:  # channel sharding: the B / C gradients are summed over ranks in the backward
             Bm, Cm = replicated_bc(Bm, Cm)
         out = S.selective_scan(inputs["u"], inputs["delta"], inputs["A"], Bm, Cm, D=inputs["D"],
-                               z=inputs["z"], delta_softplus=True)
+                               z=inputs["z"], delta_softplus=True, bc_sum=bcs)
         out.backward(inputs["dout"])
         if world > 1 and not chan:  # batch sharding: one all-reduce of the parameter gradients,
             finish_reduce()            # overlapped with the next step's forward

@@ -145,6 +145,20 @@ SSM_API int ssm_bwd(const ssm_params_t* p, ssm_stream_t stream);
 SSM_API int ssm_fwd_bidir(const ssm_params_t* fwd, const ssm_params_t* rev, ssm_stream_t stream);
 SSM_API int ssm_bwd_bidir(const ssm_params_t* fwd, const ssm_params_t* rev, ssm_stream_t stream);
 
+/* ---- backward fused with the cross-GPU sum of dB / dC (d_inner sharding) ----
+ * With the channels split across GPUs and B, C replicated, dB and dC are sums
+ * over every GPU's channels (ssmrecscan.py:158-159); ssm_bwd followed by an
+ * all-reduce of dB / dC (parallel.replicated_bc over NCCL) is the unfused form.
+ * ssm_bwd_bc_multicast instead adds this GPU's per-tile partial sums with
+ * multimem.red to `dbc_mc`, the NVLink multicast address of a float32 buffer
+ * that every participating GPU has bound: dense rows [2][batch][seqlen][16], dB
+ * rows first.  The NVSwitch applies each add to every GPU's copy.  Each GPU
+ * zeroes its own copy and all GPUs pass a cross-GPU barrier before any GPU's
+ * call; after every GPU's call and a second barrier, each copy holds the full
+ * sums.  p->dB and p->dC are not written (they may be NULL); everything else
+ * is as in ssm_bwd.  dbc_mc must be 16-byte aligned.                        */
+SSM_API int ssm_bwd_bc_multicast(const ssm_params_t* p, float* dbc_mc, ssm_stream_t stream);
+
 /* ---- causal depthwise conv1d + activation (selectssm.py:167-187) ----
  * u[b,t,c] = act( sum_{k<K} w[k,c] * xt[b, t+k-(K-1), c] ),
  * xt = x, or x flipped in L (and in channels with SSM_COMPLEMENT) with

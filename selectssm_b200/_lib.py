@@ -43,6 +43,7 @@ EXPORTED_SYMBOLS = (
     "ssm_conv1d_workspace_bytes", "ssm_conv1d_act_fwd", "ssm_conv1d_act_bwd", "ssm_strerror", "ssm_last_error",
     "ssm_version", "ssm_bwd_noalloc", "ssm_launch_count",
     "ssm_rmsnorm_workspace_bytes", "ssm_rmsnorm_fwd", "ssm_rmsnorm_bwd", "ssm_selftest_wait_timeout",
+    "ssm_bwd_bc_multicast",
 )
 
 
@@ -133,6 +134,7 @@ def load(path: str | None = None) -> ctypes.CDLL:
         "ssm_version": (ctypes.c_char_p, []),
         "ssm_launch_count": (ctypes.c_ulonglong, []),
         "ssm_bwd_noalloc": (ctypes.c_int, [P, ctypes.c_void_p]),
+        "ssm_bwd_bc_multicast": (ctypes.c_int, [P, ctypes.c_void_p, ctypes.c_void_p]),
     }
     for name, (res, args) in sigs.items():
         fn = getattr(lib, name)

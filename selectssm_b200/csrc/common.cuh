@@ -122,6 +122,15 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
+// ---------------------------------------------------------------- cross-GPU reduction
+// Adds v to the 4 floats at an NVLink multicast address: the NVSwitch applies
+// the add to the copy on every GPU bound to the multicast object.
+__device__ __forceinline__ void multimem_red_add4(float* mc, float4 v) {
+  asm volatile("multimem.red.relaxed.sys.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(mc), "f"(v.x),
+               "f"(v.y), "f"(v.z), "f"(v.w)
+               : "memory");
+}
+
 // ---------------------------------------------------------------- math
 __device__ __forceinline__ float ex2(float x) {
   float y;

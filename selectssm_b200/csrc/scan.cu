@@ -424,7 +424,7 @@ struct BwdWs {
   int64_t acc_stride;
 };
 
-static void carve_ws(const ssm_params_t* p, const Geo& g, char* ws, BwdWs* w) {
+static void carve_ws(const ssm_params_t* p, const Geo& g, char* ws, BwdWs* w, float* dbc_mc) {
   const Seg sg = choose_segments(g, kBwdSeg);
   const size_t rows = (size_t)g.B * sg.nseg * g.Dm;
   w->dA_part = reinterpret_cast<float*>(ws);
@@ -454,9 +454,15 @@ static void carve_ws(const ssm_params_t* p, const Geo& g, char* ws, BwdWs* w) {
     w->dC_acc = reinterpret_cast<float*>(p->dC);
     w->acc_stride = g.bs;
   }
+  if (dbc_mc) {  // the partial sums go to the caller's multicast buffer (dense rows)
+    w->dB_acc = dbc_mc;
+    w->dC_acc = dbc_mc + (size_t)g.B * g.L * kN;
+    w->acc_stride = kN;
+  }
 }
 
-static int fill_bwd_dir(const ssm_params_t* p, const Geo& g, const BwdWs& w, BwdDir* d, cudaStream_t s) {
+static int fill_bwd_dir(const ssm_params_t* p, const Geo& g, const BwdWs& w, BwdDir* d, cudaStream_t s,
+                        bool multicast) {
   const uint64_t es = g.es;
   if (g.bcbf16) {
     const int st = launch_widen_bc(p, g, w.Bw, w.Cw, s);
@@ -483,6 +489,7 @@ static int fill_bwd_dir(const ssm_params_t* p, const Geo& g, const BwdWs& w, Bwd
   d->dz = p->dz;
   d->dB_acc = w.dB_acc;
   d->dC_acc = w.dC_acc;
+  d->bc_mode = multicast ? kBcMulticast : kBcLocal;
   d->dA_part = w.dA_part;
   d->dD_part = w.dD_part;
   d->db_part = w.db_part;
@@ -577,7 +584,7 @@ static int launch_zero_acc(const Geo& g, const BwdWs& w, cudaStream_t s) {
   return SSM_OK;
 }
 
-static int launch_finalize(const ssm_params_t* p, const Geo& g, const BwdWs& w, cudaStream_t s) {
+static int launch_finalize(const ssm_params_t* p, const Geo& g, const BwdWs& w, cudaStream_t s, bool reduced) {
   FinalizeDir f;
   f.dA_part = w.dA_part;
   f.dD_part = w.dD_part;
@@ -594,7 +601,7 @@ static int launch_finalize(const ssm_params_t* p, const Geo& g, const BwdWs& w, 
   f.batch = g.B;
   f.L = g.L;
   f.Dm = g.Dm;
-  f.convert_bc = g.bcbf16 && (int64_t)g.B * g.L > 0;
+  f.convert_bc = g.bcbf16 && !reduced && (int64_t)g.B * g.L > 0;
   const int threads = 256;
   int64_t n = (int64_t)g.Dm * kN;
   unsigned blocks = (unsigned)((n + threads - 1) / threads);
@@ -660,9 +667,8 @@ int ssm_fwd_bidir(const ssm_params_t* fwd, const ssm_params_t* rev, ssm_stream_t
   return launch_fwd(args, rev ? 2 : 1, g, s);
 }
 
-int ssm_bwd(const ssm_params_t* p, ssm_stream_t stream) { return ssm_bwd_bidir(p, nullptr, stream); }
-
-int ssm_bwd_bidir(const ssm_params_t* fwd, const ssm_params_t* rev, ssm_stream_t stream) {
+namespace ssm {
+static int bwd_impl(const ssm_params_t* fwd, const ssm_params_t* rev, float* dbc_mc, ssm_stream_t stream) {
   Geo g, g2;
   int st = check_bwd(fwd, &g);
   if (st) return st;
@@ -679,8 +685,8 @@ int ssm_bwd_bidir(const ssm_params_t* fwd, const ssm_params_t* rev, ssm_stream_t
   if (need && (!fwd->workspace || fwd->workspace_bytes < need)) return SSM_ERR_WORKSPACE;
   if (reinterpret_cast<uintptr_t>(fwd->workspace) & 255u) return SSM_ERR_ALIGN;
   BwdWs w[2];
-  carve_ws(fwd, g, static_cast<char*>(fwd->workspace), &w[0]);
-  if (rev) carve_ws(rev, g, static_cast<char*>(fwd->workspace) + bwd_ws_bytes(g), &w[1]);
+  carve_ws(fwd, g, static_cast<char*>(fwd->workspace), &w[0], dbc_mc);
+  if (rev) carve_ws(rev, g, static_cast<char*>(fwd->workspace) + bwd_ws_bytes(g), &w[1], dbc_mc);
   const int ndir = rev ? 2 : 1;
   const ssm_params_t* ps[2] = {fwd, rev};
   if ((int64_t)g.B * g.L * g.Dm == 0) {
@@ -697,18 +703,38 @@ int ssm_bwd_bidir(const ssm_params_t* fwd, const ssm_params_t* rev, ssm_stream_t
   BwdLaunch args;
   std::memset(&args, 0, sizeof(args));
   for (int d = 0; d < ndir; ++d) {
-    st = fill_bwd_dir(ps[d], g, w[d], &args.dir[d], s);
+    st = fill_bwd_dir(ps[d], g, w[d], &args.dir[d], s, dbc_mc != nullptr);
     if (st) return st;
-    st = launch_zero_acc(g, w[d], s);
-    if (st) return st;
+    if (!dbc_mc) {  // the multicast buffer is zeroed by its owners
+      st = launch_zero_acc(g, w[d], s);
+      if (st) return st;
+    }
   }
   st = launch_bwd(args, ndir, g, s);
   if (st) return st;
   for (int d = 0; d < ndir; ++d) {
-    st = launch_finalize(ps[d], g, w[d], s);
+    st = launch_finalize(ps[d], g, w[d], s, dbc_mc != nullptr);
     if (st) return st;
   }
   return SSM_OK;
+}
+}  // namespace ssm
+
+int ssm_bwd(const ssm_params_t* p, ssm_stream_t stream) { return bwd_impl(p, nullptr, nullptr, stream); }
+
+int ssm_bwd_bidir(const ssm_params_t* fwd, const ssm_params_t* rev, ssm_stream_t stream) {
+  return bwd_impl(fwd, rev, nullptr, stream);
+}
+
+int ssm_bwd_bc_multicast(const ssm_params_t* p, float* dbc_mc, ssm_stream_t stream) {
+  if (!p || !dbc_mc) return SSM_ERR_NULL;
+  if (!aligned16(dbc_mc)) return SSM_ERR_ALIGN;
+  // dB / dC go to the multicast buffer: stand-ins keep ssm_bwd's pointer
+  // checks meaningful for everything else
+  ssm_params_t q = *p;
+  q.dB = dbc_mc;
+  q.dC = dbc_mc;
+  return bwd_impl(&q, nullptr, dbc_mc, stream);
 }
 
 const char* ssm_strerror(int status) {

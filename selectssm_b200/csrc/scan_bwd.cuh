@@ -401,11 +401,15 @@ __global__ void __launch_bounds__(kBThreads, 2) ssm_bwd_kernel(const __grid_cons
       }
       if (t < L) {
         float* dst = (q4 < 4 ? a.dB_acc : a.dC_acc) + ((size_t)b * L + t) * a.acc_stride + (q4 & 3) * 4;
-        atomicAdd(reinterpret_cast<float4*>(dst), v);
+        if (a.bc_mode == kBcMulticast)
+          multimem_red_add4(dst, v);  // the sum over GPUs, done in the NVSwitch
+        else
+          atomicAdd(reinterpret_cast<float4*>(dst), v);
       }
     }
   }
 
+  if (a.bc_mode != kBcLocal) __threadfence_system();  // dB / dC sums on other GPUs land before the kernel ends
   // release TMEM (every thread's accesses are complete)
   tmem_fence_before_sync();
   __syncthreads();

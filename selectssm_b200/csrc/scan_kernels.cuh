@@ -47,6 +47,7 @@ struct BwdDir {
   void* dz;
   float* dB_acc;   // fp32 accumulation target for dB (row stride acc_stride)
   float* dC_acc;
+  int bc_mode;     // kBcLocal / kBcMulticast
   float* dA_part;  // (B, nseg, D, 16)
   float* dD_part;  // (B, nseg, D)
   float* db_part;  // (B, nseg, D)
@@ -57,6 +58,10 @@ struct BwdDir {
   int L, Dm, flags, gate_act, has_z;
   int nseg, seg_chunks;
 };
+// How the backward accumulates its dB / dC partial sums.
+constexpr int kBcLocal = 0;      // red.add into this GPU's dB_acc / dC_acc
+constexpr int kBcMulticast = 1;  // multimem.red at dB_acc / dC_acc (NVLink multicast addresses)
+
 struct BwdLaunch {
   BwdDir dir[2];
   int zdiv;

@@ -212,7 +212,7 @@ def _workspace(p: _lib.SSMParams, device, extra=None) -> torch.Tensor:
 class _SelectiveScanFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, u, delta, A, B, C, D, z, delta_bias, delta_softplus, reverse, complement, gate_act,
-                aligned_skip):
+                aligned_skip, bc_sum=None):
         pr = _Prepared(u, delta, A, B, C, D, z, delta_bias, delta_softplus, reverse, complement, gate_act,
                        aligned_skip)
         out = torch.empty(pr.shape, dtype=pr.dtype, device=pr.u.device)
@@ -222,6 +222,7 @@ class _SelectiveScanFn(torch.autograd.Function):
         _lib.check(_lib.load().ssm_fwd(ctypes_byref(p), _stream()), "ssm_fwd")
         del ws
         ctx.pr = pr
+        ctx.bc_sum = bc_sum
         ctx.delta_broadcast = delta.shape[-1] == 1 and u.shape[-1] != 1
         ctx.save_for_backward(states)
         return out
@@ -234,13 +235,18 @@ class _SelectiveScanFn(torch.autograd.Function):
         p = pr.params(states=states)
         g = pr.grads(p, dout, pr.shape[2])
         ws = _workspace(p, pr.u.device)
-        _lib.check(_lib.load().ssm_bwd(ctypes_byref(p), _stream()), "ssm_bwd")
+        if ctx.bc_sum is None:
+            _lib.check(_lib.load().ssm_bwd(ctypes_byref(p), _stream()), "ssm_bwd")
+        else:  # dB / dC summed over the channel shards inside the kernel
+            mc = ctx.bc_sum.begin(pr.shape[0], pr.shape[1])
+            _lib.check(_lib.load().ssm_bwd_bc_multicast(ctypes_byref(p), mc, _stream()), "ssm_bwd_bc_multicast")
+            g["dB"], g["dC"] = ctx.bc_sum.end(pr.B.dtype)
         del ws
         ddelta = g["ddelta"]
         if ctx.delta_broadcast:
             ddelta = ddelta.sum(-1, keepdim=True)
         return (g["du"], ddelta, g["dA"], g["dB"], g["dC"], g["dD"], g["dz"], g["ddelta_bias"],
-                None, None, None, None, None)
+                None, None, None, None, None, None)
 
 
 def ctypes_byref(p):
@@ -249,7 +255,7 @@ def ctypes_byref(p):
 
 
 def selective_scan(u, delta, A, B, C, D=None, z=None, delta_bias=None, delta_softplus=False, reverse=False,
-                   complement=False, gate_act="silu", aligned_skip=False):
+                   complement=False, gate_act="silu", aligned_skip=False, bc_sum=None):
     """Fused selective scan on CUDA tensors (differentiable).
 
     u, delta: (batch, L, dim) in the scan frame; A: (dim, 16) fp32; B, C:
@@ -259,9 +265,14 @@ def selective_scan(u, delta, A, B, C, D=None, z=None, delta_bias=None, delta_sof
     ``reverse``/``complement`` follow SelectiveSSM (selectssm.py:115-116, 167-168,
     230-231); the skip adds the scan-frame ``u * D`` unflipped, as the reference
     does at selectssm.py:238, unless ``aligned_skip``.
+
+    ``bc_sum`` (a ``parallel.MulticastBCSum``) is for d_inner sharding with B
+    and C replicated: the backward kernel then sums dB / dC over the group's
+    ranks through NVLink multicast, so the returned B / C gradients are the
+    totals (do not also wrap B, C in ``parallel.replicated_bc``).
     """
     return _SelectiveScanFn.apply(u, delta, A, B, C, D, z, delta_bias, bool(delta_softplus), bool(reverse),
-                                  bool(complement), gate_act, bool(aligned_skip))
+                                  bool(complement), gate_act, bool(aligned_skip), bc_sum)
 
 
 # ----------------------------------------------------------------------------- reference API

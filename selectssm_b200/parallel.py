@@ -13,6 +13,8 @@ shared by all channels of a batch row):
   dt-bias gradient are per channel and stay local, but dB and dC are sums over
   all channels (src/selectssm/ssmrecscan.py:158-159), so their gradient is
   all-reduced in the backward -- ``replicated_bc`` inserts that reduction.
+  ``MulticastBCSum`` fuses it into the backward kernel instead: partial sums go
+  to every rank's copy through NVLink multicast (``multimem.red``).
 
 Collectives use whatever backend the default process group has (NCCL over
 NVLink on the B200 box; gloo in the CPU tests).
@@ -81,6 +83,59 @@ class _SumGradsAcrossRanks(torch.autograd.Function):
             out.append(flat[off:off + g.numel()].view_as(g))
             off += g.numel()
         return (None,) + tuple(out)
+
+
+class MulticastBCSum:
+    """dB / dC of a d_inner-sharded scan, summed over ranks inside the backward
+    kernel (``ssm_bwd_bc_multicast``) instead of by an all-reduce after it.
+
+    A float32 buffer of 2 x (batch, seqlen, 16) is allocated in symmetric
+    memory and bound to an NVLink multicast object; the kernel adds each
+    tile's partial sums with ``multimem.red``, which the NVSwitch applies to
+    every rank's copy.  Each backward: zero the local copy, a stream-ordered
+    barrier (a one-element NCCL all-reduce), the kernel, a second barrier, then
+    read the local copy.  ``available`` is False where the GPUs have no
+    multicast support (then use ``replicated_bc``).  Collective: every rank of
+    ``group`` constructs it with the same shape, and every rank's backward
+    must run it (the barriers pair up across ranks).
+    """
+
+    def __init__(self, batch: int, seqlen: int, group=None, device=None):
+        import torch.distributed._symmetric_memory as symm_mem
+        self.group = group if group is not None else dist.group.WORLD
+        self.shape = (batch, seqlen, 16)
+        n = batch * seqlen * 16
+        self.buf = symm_mem.empty(2 * n, dtype=torch.float32, device=device)
+        self.handle = symm_mem.rendezvous(self.buf, self.group)
+        self.mc = int(self.handle.multicast_ptr)
+        self._flag = torch.zeros(1, dtype=torch.float32, device=self.buf.device)
+
+    @property
+    def available(self) -> bool:
+        return self.mc != 0
+
+    def _barrier(self):
+        # synchronous NCCL collective: the current stream waits for it, and it
+        # completes only after every rank's stream reached it
+        dist.all_reduce(self._flag, group=self.group)
+
+    def begin(self, batch: int, seqlen: int) -> int:
+        """Zero this rank's copy, wait for every rank to do so, and return the
+        multicast address for the kernel."""
+        if (batch, seqlen, 16) != self.shape:
+            raise ValueError(f"MulticastBCSum was made for {self.shape[:2]}, the scan has {(batch, seqlen)}")
+        if not self.available:
+            raise RuntimeError("no NVLink multicast on this group; use parallel.replicated_bc")
+        self.buf.zero_()
+        self._barrier()
+        return self.mc
+
+    def end(self, dtype):
+        """Wait for every rank's kernel; return (dB, dC) totals in ``dtype``."""
+        self._barrier()
+        n = self.buf.numel() // 2
+        return (self.buf[:n].view(self.shape).to(dtype, copy=True),
+                self.buf[n:].view(self.shape).to(dtype, copy=True))
 
 
 def replicated_bc(Bm: torch.Tensor, Cm: torch.Tensor, group=None):
