@@ -508,7 +508,7 @@ def main():
                 "traffic": read_traffic("ssm_bwd_kernel_config2.md"), "algorithmic_bytes": bb,
                 "ms": t_bwd}
     roof_bwd["frac"] = roof_bwd["achieved"] / hbm
-    roof_fwd = {"kernel": "ssm_fwd call: ssm_fwd_kernel<float,float,0> (+ segment pre-pass when segmented)", "bound": "hbm", "achieved": fb / (t_fwd * 1e-3) / 1e9,
+    roof_fwd = {"kernel": "ssm_fwd call: ssm_fwd_kernel<float,float,0,1> (+ segment pre-pass when segmented)", "bound": "hbm", "achieved": fb / (t_fwd * 1e-3) / 1e9,
                 "peak": hbm, "unit": "GB/s", "traffic": read_traffic("ssm_fwd_kernel_config2.md"),
                 "algorithmic_bytes": fb, "ms": t_fwd}
     roof_fwd["frac"] = roof_fwd["achieved"] / hbm

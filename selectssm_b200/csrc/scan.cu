@@ -401,11 +401,12 @@ static int launch_fwd_t(FwdLaunch& L, int ndir, const Geo& g, cudaStream_t s) {
     note_launches(1);
   SSM_CUDA_CHECK(cudaGetLastError(), "launch ssm_fwd_kernel<agg>");
   }
-  auto kern = ssm_fwd_kernel<T, TBC, false>;
-  SSM_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kBytes),
-                 "cudaFuncSetAttribute(ssm_fwd_kernel)");
   L.zdiv = nseg;
   grid.z = ndir * nseg;
+  const bool wide = (long)grid.x * grid.y * grid.z <= 3L * kSMs;
+  auto kern = wide ? ssm_fwd_kernel<T, TBC, false, true> : ssm_fwd_kernel<T, TBC, false, false>;
+  SSM_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kBytes),
+                 "cudaFuncSetAttribute(ssm_fwd_kernel)");
   kern<<<grid, kFThreads, kBytes, s>>>(L);
   note_launches(1);
   SSM_CUDA_CHECK(cudaGetLastError(), "launch ssm_fwd_kernel");

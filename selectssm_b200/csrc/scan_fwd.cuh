@@ -51,8 +51,10 @@ struct FwdSmem {
 };
 
 
-template <typename T, typename TBC, bool AGG>
-__global__ void __launch_bounds__(kFThreads, 6) ssm_fwd_kernel(const __grid_constant__ FwdLaunch P) {
+// WIDE: the grid fills at most 3 CTAs per SM, so each thread may use up to 168
+// registers (more scheduling freedom); otherwise 6 CTAs per SM fit (80).
+template <typename T, typename TBC, bool AGG, bool WIDE = false>
+__global__ void __launch_bounds__(kFThreads, WIDE ? 3 : 6) ssm_fwd_kernel(const __grid_constant__ FwdLaunch P) {
   using S = FwdSmem<T, TBC>;
   const FwdDir& a = P.dir[blockIdx.z / P.zdiv];
   const int seg = blockIdx.z % P.zdiv;
