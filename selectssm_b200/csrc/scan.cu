@@ -540,7 +540,7 @@ static int launch_bwd_t(BwdLaunch& L, int ndir, const Geo& g, cudaStream_t s) {
     note_launches(1);
   SSM_CUDA_CHECK(cudaGetLastError(), "launch ssm_bwd_fold_kernel");
   }
-  auto kern = ssm_bwd_kernel<T, TBC, G>;
+  auto kern = L.dir[0].bc_mode == kBcMulticast ? ssm_bwd_kernel<T, TBC, G, true> : ssm_bwd_kernel<T, TBC, G, false>;
   SSM_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes),
                  "cudaFuncSetAttribute(ssm_bwd_kernel)");
   L.zdiv = nseg;

@@ -137,7 +137,9 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
 
 // G: the gate activation (an ssm_act code), fixed per launch so the step loops
 // hold no branch on it.
-template <typename T, typename TBC, int G>
+// MC: dB / dC partial sums go to NVLink multicast addresses (cross-GPU sum);
+// a template parameter so the single-GPU instance carries no trace of it.
+template <typename T, typename TBC, int G, bool MC = false>
 __global__ void __launch_bounds__(kBThreads, 2) ssm_bwd_kernel(const __grid_constant__ BwdLaunch P) {
   const BwdDir& a = P.dir[blockIdx.z / P.zdiv];
   const int seg = blockIdx.z % P.zdiv;
@@ -401,7 +403,7 @@ __global__ void __launch_bounds__(kBThreads, 2) ssm_bwd_kernel(const __grid_cons
       }
       if (t < L) {
         float* dst = (q4 < 4 ? a.dB_acc : a.dC_acc) + ((size_t)b * L + t) * a.acc_stride + (q4 & 3) * 4;
-        if (a.bc_mode == kBcMulticast)
+        if constexpr (MC)
           multimem_red_add4(dst, v);  // the sum over GPUs, done in the NVSwitch
         else
           atomicAdd(reinterpret_cast<float4*>(dst), v);
@@ -409,7 +411,7 @@ __global__ void __launch_bounds__(kBThreads, 2) ssm_bwd_kernel(const __grid_cons
     }
   }
 
-  if (a.bc_mode != kBcLocal) __threadfence_system();  // dB / dC sums on other GPUs land before the kernel ends
+  if constexpr (MC) __threadfence_system();  // dB / dC sums on other GPUs land before the kernel ends
   // release TMEM (every thread's accesses are complete)
   tmem_fence_before_sync();
   __syncthreads();
