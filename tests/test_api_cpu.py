@@ -98,3 +98,29 @@ def test_module_parameters_use_flax_names_and_layouts():
         BidirectionalMamba(64, 16, 2.0, activation="tanh")
     with pytest.raises(ValueError, match="chunk_size"):
         SelectiveSSM(64, chunk_size=7)(torch.zeros(1, 32, 64))
+
+
+def test_workspace_covers_widened_bc_and_bidirectional_segments():
+    """bf16 B/C need room for their float32 copies (2 x B*L*16*4 bytes) on top
+    of the fp32 case's scratch, and one parameter set's size already covers a
+    bidirectional launch (its segment count may differ)."""
+    lib = _lib.load()
+
+    def ws(bc, B=2, L=131072, D=512):
+        p = _lib.SSMParams()
+        p.batch, p.seqlen, p.dim, p.dstate = B, L, D, 16
+        p.dtype, p.bc_dtype = _lib.SSM_BF16, bc
+        return lib.ssm_workspace_bytes(ctypes.byref(p))
+
+    f32, b16 = ws(_lib.SSM_F32), ws(_lib.SSM_BF16)
+    assert f32 > 0 and b16 >= f32 + 2 * 2 * 131072 * 16 * 4
+
+
+def test_multicast_backward_validates_arguments_without_gpu():
+    lib = _lib.load()
+    p = _lib.SSMParams()
+    p.batch, p.seqlen, p.dim, p.dstate = 2, 16, 32, 16
+    assert lib.ssm_bwd_bc_multicast(ctypes.byref(p), None, None) == _lib.SSM_ERR_NULL
+    assert lib.ssm_bwd_bc_multicast(ctypes.byref(p), 0x1008, None) == _lib.SSM_ERR_ALIGN
+    p.dstate = 8
+    assert lib.ssm_bwd_bc_multicast(ctypes.byref(p), 0x1000, None) == _lib.SSM_ERR_SHAPE
