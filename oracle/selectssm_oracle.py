@@ -258,15 +258,64 @@ def ssm_scan_sequential(x, A, B, C, Delta, h0=None, return_states=False):
     return (y, states) if return_states else y
 
 
+def ssm_scan_final_state(x, A, B, C, Delta, h0=None, chunk=256):
+    """State after the last step of h_t = exp(A dt_t) h_{t-1} + dt_t B_t x_t from
+    ``h0`` (zeros by default).  Chunks of ``chunk`` steps are composed with the
+    carry rule of selectssm.py:87-91: within a chunk,
+    h_T = exp(A S_T) h_0 + sum_t exp(A (S_T - S_t)) dt_t B_t x_t, S_t the
+    running sum of dt, so long sequences need no per-step Python loop."""
+    Bsz, L, D = x.shape
+    N = A.shape[-1]
+    Delta = np.broadcast_to(Delta, x.shape)
+    h = np.zeros((Bsz, D, N), np.float64) if h0 is None else np.array(h0, np.float64)
+    for t0 in range(0, L, chunk):
+        sl = slice(t0, min(L, t0 + chunk))
+        dt = Delta[:, sl].astype(np.float64)
+        S = np.cumsum(dt, axis=1)                                   # (B,T,D)
+        ST = S[:, -1]                                               # (B,D)
+        w = np.exp(A[None, None] * (ST[:, None] - S)[..., None])    # (B,T,D,N)
+        beta = (dt * x[:, sl])[..., None] * B[:, sl, None, :]
+        h = np.exp(A[None] * ST[..., None]) * h + (w * beta).sum(axis=1)
+    return h
+
+
+def ssm_scan_adjoint_carry(A, C, Delta, dy, fa0=None, chunk=256):
+    """Adjoint carried out of the first step, f_0 alpha_0, of the reverse
+    recurrence f_t = f_{t+1} alpha_{t+1} + C_t dy_t (backward_scan_fn,
+    ssmrecscan.py:96-100) run over the whole sequence from the carry ``fa0``
+    (zeros by default), alpha_t = exp(A dt_t).  Chunked like
+    :func:`ssm_scan_final_state`: f_0 alpha_0 = exp(A S_T) fa0 +
+    sum_t exp(A S_t) C_t dy_t with S_t the sum of dt over steps 0..t."""
+    Bsz, L, D = dy.shape
+    N = A.shape[-1]
+    Delta = np.broadcast_to(Delta, dy.shape)
+    fa = np.zeros((Bsz, D, N), np.float64) if fa0 is None else np.array(fa0, np.float64)
+    starts = list(range(0, L, chunk))
+    for t0 in reversed(starts):
+        sl = slice(t0, min(L, t0 + chunk))
+        dt = Delta[:, sl].astype(np.float64)
+        S = np.cumsum(dt, axis=1)
+        w = np.exp(A[None, None] * S[..., None])                    # (B,T,D,N)
+        cdy = dy[:, sl, :, None] * C[:, sl, None, :]
+        fa = np.exp(A[None] * S[:, -1, :, None]) * fa + (w * cdy).sum(axis=1)
+    return fa
+
+
 # ----------------------------------------------------------------------------
 # custom-VJP backward (ssmrecscan.py:90-181)
 # ----------------------------------------------------------------------------
 
 
-def ssm_scan_backward(x, A, B, C, Delta, dy, min_recursion_length=2, recursive_split=2):
+def ssm_scan_backward(x, A, B, C, Delta, dy, min_recursion_length=2, recursive_split=2,
+                      h_left=None, f_alpha_right=None):
     """Restates ssm_scan_backward / ssm_scan_backward_recursive.
 
     Returns (dx, dA, dB, dC, dDelta) in the (B,L,.) layout (ssmrecscan.py:163-181).
+    ``h_left`` (B,D,N) is the state entering the first step and ``f_alpha_right``
+    (B,D,N) the adjoint carried in from beyond the last step, the two carries
+    ssm_scan_backward_recursive takes (ssmrecscan.py:111); the top level passes
+    zeros for both (:174-175), which is the default here.  Non-zero carries
+    let a window of a long sequence be checked on its own.
     """
     Bsz, L, D = x.shape
     N = A.shape[-1]
@@ -332,7 +381,9 @@ def ssm_scan_backward(x, A, B, C, Delta, dy, min_recursion_length=2, recursive_s
         return dx, dA, dB, dC, dDelta, h_right
 
     z = np.zeros((Bsz, D, N), x.dtype)
-    dx, dA, dB, dC, dDelta, _ = rec(xt, Bt, Ct, Dt, dyt, z, z.copy())
+    hl = z if h_left is None else np.asarray(h_left, x.dtype)
+    fr = z.copy() if f_alpha_right is None else np.asarray(f_alpha_right, x.dtype)
+    dx, dA, dB, dC, dDelta, _ = rec(xt, Bt, Ct, Dt, dyt, hl, fr)
     t = lambda a: a.transpose(1, 0, 2)
     return t(dx), dA, t(dB), t(dC), t(dDelta)
 
@@ -351,7 +402,7 @@ def _flip_out(a, reverse, complement):
 
 def selective_scan_fwd(u, delta, A, B, C, D=None, z=None, delta_bias=None,
                        delta_softplus=False, reverse=False, complement=False,
-                       gate_act="silu", aligned_skip=False, return_aux=False):
+                       gate_act="silu", aligned_skip=False, return_aux=False, h0=None):
     """Fused op the CUDA forward computes.
 
     u, delta, B, C are in the scan frame (for ``reverse`` they are the tensors
@@ -364,11 +415,13 @@ def selective_scan_fwd(u, delta, A, B, C, D=None, z=None, delta_bias=None,
 
     with y_scan the scan of (u, A, B, C, dt), dt = softplus(delta + bias)
     (selectssm.py:204-210).  The gate is BidirectionalMamba's y * act(z)
-    (selectssm.py:336).
+    (selectssm.py:336).  ``h0`` (B,D,N), the state entering the first
+    scan-frame step, is zero for a whole sequence; a window of a longer one
+    passes the state carried into it.
     """
     dt_pre = delta if delta_bias is None else delta + delta_bias
     dt = softplus(dt_pre) if delta_softplus else dt_pre
-    ys = ssm_scan_sequential(u, A, B, C, dt)
+    ys = ssm_scan_sequential(u, A, B, C, dt, h0=h0)
     y = _flip_out(ys, reverse, complement).copy()
     if D is not None:
         if aligned_skip:
@@ -384,12 +437,14 @@ def selective_scan_fwd(u, delta, A, B, C, D=None, z=None, delta_bias=None,
 
 def selective_scan_bwd(u, delta, A, B, C, dout, D=None, z=None, delta_bias=None,
                        delta_softplus=False, reverse=False, complement=False,
-                       gate_act="silu", aligned_skip=False):
+                       gate_act="silu", aligned_skip=False, h0=None, fa_right=None):
     """Gradients of :func:`selective_scan_fwd`.  Returns a dict with du, ddelta,
     dA, dB, dC, dD, ddelta_bias, dz.  The scan part follows the custom-VJP leaf
-    formulas (ssmrecscan.py:150-161) on a single leaf."""
+    formulas (ssmrecscan.py:150-161) on a single leaf.  ``h0`` and ``fa_right``
+    are the scan-frame carries of a window (state entering its first step,
+    adjoint f alpha entering from beyond its last step); zero by default."""
     out, aux = selective_scan_fwd(u, delta, A, B, C, D, z, delta_bias, delta_softplus,
-                                  reverse, complement, gate_act, aligned_skip, return_aux=True)
+                                  reverse, complement, gate_act, aligned_skip, return_aux=True, h0=h0)
     dt, dt_pre, ys, pre = aux["dt"], aux["dt_pre"], aux["ys"], aux["pre_gate"]
     res = {}
     if z is not None:
@@ -399,7 +454,8 @@ def selective_scan_bwd(u, delta, A, B, C, dout, D=None, z=None, delta_bias=None,
         dpre = dout
         res["dz"] = None
     dys = _flip_out(dpre, reverse, complement)  # involution
-    dx, dA, dB, dC, ddt = ssm_scan_backward(u, A, B, C, dt, dys, min_recursion_length=u.shape[1] + 1)
+    dx, dA, dB, dC, ddt = ssm_scan_backward(u, A, B, C, dt, dys, min_recursion_length=u.shape[1] + 1,
+                                            h_left=h0, f_alpha_right=fa_right)
     du = dx.copy()
     if D is not None:
         if aligned_skip:

@@ -20,7 +20,7 @@ functions, e.g. ``selectssm.selectssm.ssm_chunked_scan = jax_ffi.ssm_chunked_sca
 Setup in a JAX environment: ``build_handlers()`` once (compiles
 ``csrc/jax_ffi_handlers.cc`` against ``jax.ffi.include_dir()``), then
 ``register()`` before tracing.  JAX is imported lazily, so importing this
-module without JAX works (and does nothing).
+module without JAX works (and does nothing).  Nothing here imports PyTorch.
 """
 
 from __future__ import annotations
@@ -31,7 +31,7 @@ import os
 import subprocess
 
 from . import _lib
-from .ops import _check_chunked, largest_factor_up_to  # noqa: F401  (same ValueErrors as the reference)
+from ._checks import check_chunked as _check_chunked, largest_factor_up_to  # noqa: F401  (same ValueErrors)
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 HANDLER_SRC = os.path.join(HERE, "csrc", "jax_ffi_handlers.cc")

@@ -20,26 +20,15 @@ extended op :func:`selective_scan` adds the softplus(dt + bias) preamble
 
 from __future__ import annotations
 
-import math
-
 import torch
 
 from . import _lib
+from ._checks import check_chunked as _check_chunked, largest_factor_up_to  # noqa: F401
 
 __all__ = [
     "selective_scan", "selective_scan_bidir", "ssm_chunked_scan", "ssm_recursive_scan", "ssm_scan",
     "conv1d_act", "largest_factor_up_to",
 ]
-
-
-def largest_factor_up_to(b, n):
-    """selectssm.py:24-30: largest k <= b dividing n (n itself when n < 2)."""
-    if n < 2:
-        return n
-    k = b
-    while n % k != 0:
-        k -= 1
-    return k
 
 
 # ----------------------------------------------------------------------------- helpers
@@ -276,18 +265,6 @@ def selective_scan(u, delta, A, B, C, D=None, z=None, delta_bias=None, delta_sof
 
 
 # ----------------------------------------------------------------------------- reference API
-def _check_chunked(L, D, chunk_size, n_channel_groups):
-    """The ValueErrors of selectssm.py:47-48 and :53-54."""
-    K = 1 if n_channel_groups is None else n_channel_groups
-    if D % K != 0:
-        raise ValueError(f"n_channel_groups={n_channel_groups} must divide D={D}")
-    if chunk_size is None:
-        chunk_size = largest_factor_up_to(int(math.sqrt(K * L)), L)
-    if L % chunk_size != 0:
-        raise ValueError(f"chunk_size={chunk_size} must divide L={L}")
-    return chunk_size
-
-
 def ssm_chunked_scan(x, Acoeff, Bcoeff, Ccoeff, dt, chunk_size: int = None, n_channel_groups: int = 1):
     """Drop-in for selectssm.ssm_chunked_scan (selectssm.py:37-109).
 

@@ -114,6 +114,33 @@ def check_bc_linearity(t, g, groups, tol, **kw):
     assert rel(npy(g["C"]), npy(dC)) < tol, "dC"
 
 
+def _np_slice(t, s, e, ch=None):
+    v = t[:, s:e]
+    if ch is not None:
+        v = v.index_select(-1, ch)
+    return npy(v)
+
+
+def carry_in(u, dt_fn, delta, A, B, t0, ch, block=16384):
+    """Scan-frame state entering step t0 (oracle, float64), from [0, t0) read in blocks."""
+    h = None
+    for s in range(0, t0, block):
+        e = min(t0, s + block)
+        h = O.ssm_scan_final_state(_np_slice(u, s, e, ch), A, _np_slice(B, s, e), None,
+                                   dt_fn(_np_slice(delta, s, e, ch)), h0=h)
+    return h
+
+
+def carry_right(dys_fn, delta, dt_fn, A, C, t1, L, ch, block=16384):
+    """Adjoint f alpha entering step t1 - 1 from the right (oracle), from [t1, L) in blocks."""
+    fa = None
+    for s in reversed(range(t1, L, block)):
+        e = min(L, s + block)
+        fa = O.ssm_scan_adjoint_carry(A, _np_slice(C, s, e), dt_fn(_np_slice(delta, s, e, ch)), dys_fn(s, e),
+                                      fa0=fa)
+    return fa
+
+
 def groups_sym(D, n):
     """n complement-closed groups covering all D channels."""
     k = D // (2 * n)
@@ -172,6 +199,36 @@ def test_config3_bidirectional_complement_bf16(cuda):
     # the shared z collects both directions' dz
     assert rel(npy(zt.grad.index_select(-1, idx)), dz_ref) < tol
 
+    # dB / dC (sums over all 512 channels) of batch row 0, both directions, on a
+    # window of the scan frame with the state and adjoint carried into it from
+    # the rest of the row by the oracle
+    L = 131072
+    t0, t1 = 70000, 71024
+    act = lambda v: v * O.sigmoid(v)  # noqa: E731  silu gate
+    for half, (d, leaves) in enumerate(((f, lf), (r, lr))):
+        bias = npy(d["bias"])
+        dt_fn = lambda v: O.softplus(v + bias)  # noqa: E731
+        A = npy(d["A"])
+
+        def dys(s, e, half=half):
+            # scan-frame upstream gradient of y on scan steps [s, e); the reverse
+            # direction with complement reads output step L-1-t, channel D-1-c
+            if half == 0:
+                return npy(dout[:1, s:e, :Dm]) * act(npy(zt[:1, s:e]))
+            o0, o1 = L - e, L - s
+            v = npy(dout[:1, o0:o1, Dm:]) * act(npy(zt[:1, o0:o1]))
+            return v[:, ::-1, ::-1].copy()
+
+        row = {k: d[k][:1] for k in ("u", "delta", "B", "C")}
+        h0 = carry_in(row["u"], dt_fn, row["delta"], A, row["B"], t0, None)
+        fa = carry_right(dys, row["delta"], dt_fn, A, row["C"], t1, L, None)
+        a = {k: _np_slice(v, t0, t1) for k, v in row.items()}
+        gw = O.selective_scan_bwd(a["u"], a["delta"], A, a["B"], a["C"], dys(t0, t1), delta_bias=bias,
+                                  delta_softplus=True, h0=h0, fa_right=fa)
+        g = dict(zip(names, (x.grad for x in leaves)))
+        assert rel(npy(g["B"][:1, t0:t1]), gw["dB"]) < tol, (half, "dB")
+        assert rel(npy(g["C"][:1, t0:t1]), gw["dC"]) < tol, (half, "dC")
+
 
 @pytest.mark.timeout(900)
 def test_config4_long_sequence_channel_shards(cuda):
@@ -196,6 +253,30 @@ def test_config4_long_sequence_channel_shards(cuda):
         del so, sg
     assert rel_t(g["B"], dB) < 1e-5
     assert rel_t(g["C"], dC) < 1e-5
+    # backward (and forward) of 4 channels on a window in the middle of the
+    # sequence, against the oracle with the state and the adjoint carried into
+    # the window from the rest of the sequence (ssm_scan_backward_recursive's
+    # h_left / f_alpha_right, ssmrecscan.py:111)
+    ch = torch.tensor([5, 130, 641, 1022], device=cuda)
+    t0, t1 = 524_288 + 3_001, 524_288 + 5_049
+    A = npy(t["A"].index_select(0, ch))
+    bias = npy(t["bias"].index_select(0, ch))
+    Dv = npy(t["D"].index_select(0, ch))
+    dt_fn = lambda v: O.softplus(v + bias)  # noqa: E731
+    silu = lambda v: v * O.sigmoid(v)  # noqa: E731
+    dys = lambda s, e: _np_slice(t["dout"], s, e, ch) * silu(_np_slice(t["z"], s, e, ch))  # noqa: E731
+    h0 = carry_in(t["u"], dt_fn, t["delta"], A, t["B"], t0, ch)
+    fa = carry_right(dys, t["delta"], dt_fn, A, t["C"], t1, L, ch)
+    w = {k: _np_slice(t[k], t0, t1, ch) for k in ACT}
+    wB, wC = _np_slice(t["B"], t0, t1), _np_slice(t["C"], t0, t1)
+    okw = dict(D=Dv, z=w["z"], delta_bias=bias, delta_softplus=True, h0=h0)
+    ref_out = O.selective_scan_fwd(w["u"], w["delta"], A, wB, wC, **okw)
+    ref = O.selective_scan_bwd(w["u"], w["delta"], A, wB, wC, w["dout"], fa_right=fa, **okw)
+    assert rel(_np_slice(out, t0, t1, ch), ref_out) < 1e-4, "window out"
+    for name, k in (("du", "u"), ("ddelta", "delta"), ("dz", "z")):
+        e = rel(_np_slice(g[k], t0, t1, ch), ref[name])
+        assert e < 1e-4, ("window", name, e)
+
     # forward on 4 channels against the oracle's chunked scan (raw scan: no skip, gate or softplus)
     import selectssm_b200 as S
     idx = torch.tensor([3, 500, 777, 1000], device=cuda)

@@ -30,3 +30,25 @@ def test_handler_source_matches_header_and_targets():
 def test_jax_path_when_available():
     pytest.importorskip("jax")
     from selectssm_b200 import jax_ffi  # noqa: F401  (exercised only where JAX exists)
+
+
+def test_jax_binding_imports_without_torch():
+    """The JAX host path needs no PyTorch: importing the binding in a process
+    where ``import torch`` fails still works, and keeps the reference's
+    ValueErrors (selectssm.py:47-48, :53-54)."""
+    import subprocess
+    import sys
+    code = (
+        "import sys; sys.modules['torch'] = None\n"
+        "from selectssm_b200 import jax_ffi\n"
+        "assert jax_ffi.largest_factor_up_to(64, 1024) == 64\n"
+        "try:\n"
+        "    jax_ffi._check_chunked(1000, 8, 64, 1)\n"
+        "except ValueError:\n"
+        "    pass\n"
+        "else:\n"
+        "    raise SystemExit('no ValueError')\n"
+        "assert 'torch' not in [m for m in sys.modules if sys.modules[m] is not None]\n"
+        "print('ok')\n")
+    r = subprocess.run([sys.executable, "-c", code], cwd=ROOT, capture_output=True, text=True, timeout=120)
+    assert r.returncode == 0 and "ok" in r.stdout, r.stderr

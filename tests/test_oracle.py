@@ -124,3 +124,59 @@ def test_reverse_skip_frame_quirk():
     assert rel(a, ys[:, ::-1] + inp["u"] * inp["D"]) < 1e-12
     assert rel(b, (ys + inp["u"] * inp["D"])[:, ::-1]) < 1e-12
     assert rel(a, b) > 1e-3
+
+
+def test_carry_helpers_match_sequential():
+    """The chunked final-state and adjoint-carry helpers equal the per-step
+    recurrences (forward_scan_fn / backward_scan_fn, ssmrecscan.py:90-100)."""
+    inp = O.make_scan_inputs(2, 200, 5, 16, seed=7)
+    dt = O.softplus(inp["delta"])
+    y, hs = O.ssm_scan_sequential(inp["u"], inp["A"], inp["B"], inp["C"], dt, return_states=True)
+    h = O.ssm_scan_final_state(inp["u"], inp["A"], inp["B"], inp["C"], dt, chunk=64)
+    assert np.abs(h - hs[:, -1]).max() <= 1e-12 * np.abs(hs[:, -1]).max()
+    fa = np.zeros((2, 5, 16))
+    alpha = np.exp(inp["A"][None, None] * dt[..., None])
+    cdy = inp["dout"][..., None] * inp["C"][:, :, None, :]
+    for t in range(199, -1, -1):
+        fa = (fa + cdy[:, t]) * alpha[:, t]
+    got = O.ssm_scan_adjoint_carry(inp["A"], inp["C"], dt, inp["dout"], chunk=48)
+    assert np.abs(got - fa).max() <= 1e-12 * np.abs(fa).max()
+
+
+@pytest.mark.parametrize("reverse,complement", [(False, False), (True, True)])
+def test_window_with_carries_matches_whole_sequence(reverse, complement):
+    """A window [t0, t1) of the scan frame, run with the state carried into it
+    and the adjoint carried in from its right, reproduces the whole-sequence
+    outputs and per-step gradients on the window (the leaf carries of
+    ssm_scan_backward_recursive, ssmrecscan.py:111)."""
+    L, t0, t1 = 96, 40, 72
+    inp = O.make_scan_inputs(2, L, 6, 16, seed=3)
+    kw = dict(D=inp["D"], z=inp["z"], delta_softplus=True, reverse=reverse, complement=complement)
+    args = (inp["u"], inp["delta"], inp["A"], inp["B"], inp["C"])
+    out = O.selective_scan_fwd(*args, **kw)
+    g = O.selective_scan_bwd(*args, inp["dout"], **kw)
+    flip = (lambda a: a[:, ::-1, ::-1] if complement else a[:, ::-1]) if reverse else (lambda a: a)
+    # window carries from the scan-frame data (output-frame tensors flipped into the scan frame)
+    dt = O.softplus(inp["delta"])
+    dys = flip(inp["dout"] * O.activation(inp["z"], "silu"))
+    h0 = O.ssm_scan_final_state(inp["u"][:, :t0], inp["A"], inp["B"][:, :t0], inp["C"][:, :t0], dt[:, :t0])
+    fa = O.ssm_scan_adjoint_carry(inp["A"], inp["C"][:, t1:], dt[:, t1:], dys[:, t1:])
+    win = lambda a: a[:, t0:t1]
+    if reverse:
+        # the reverse direction's window is a window of its scan frame: check the raw scan
+        # there, driven by the scan-frame upstream gradient
+        wkw = dict(D=None, z=None, delta_softplus=True)
+        gw = O.selective_scan_bwd(win(inp["u"]), win(inp["delta"]), inp["A"], win(inp["B"]), win(inp["C"]),
+                                  win(dys), h0=h0, fa_right=fa, **wkw)
+        gf = O.selective_scan_bwd(*args, dys, **wkw)
+        for k in ("du", "ddelta", "dB", "dC"):
+            assert np.abs(gw[k] - win(gf[k])).max() <= 1e-10 * np.abs(gf[k]).max(), k
+        return
+    ow = O.selective_scan_fwd(win(inp["u"]), win(inp["delta"]), inp["A"], win(inp["B"]), win(inp["C"]),
+                              D=inp["D"], z=win(inp["z"]), delta_softplus=True, h0=h0)
+    assert np.abs(ow - win(out)).max() <= 1e-10 * np.abs(out).max()
+    gw = O.selective_scan_bwd(win(inp["u"]), win(inp["delta"]), inp["A"], win(inp["B"]), win(inp["C"]),
+                              win(inp["dout"]), D=inp["D"], z=win(inp["z"]), delta_softplus=True, h0=h0,
+                              fa_right=fa)
+    for k in ("du", "ddelta", "dz", "dB", "dC"):
+        assert np.abs(gw[k] - win(g[k])).max() <= 1e-10 * np.abs(g[k]).max(), k
