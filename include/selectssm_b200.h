@@ -125,13 +125,21 @@ typedef struct ssm_params {
  * params: the forward uses it when it splits the sequence into segments, the
  * backward always; one buffer of this size serves both calls. */
 SSM_API size_t ssm_workspace_bytes(const ssm_params_t* p);
+/* Bytes of scratch a single-direction backward needs for these params: ssm_bwd
+ * (multicast = 0) or ssm_bwd_bc_multicast (multicast = 1, which keeps no dB /
+ * dC partials of its own).  Never more than ssm_workspace_bytes(p). */
+SSM_API size_t ssm_bwd_workspace_bytes(const ssm_params_t* p, int multicast);
+/* Bytes of scratch ssm_fwd needs for these params (0 when it needs none). */
+SSM_API size_t ssm_fwd_workspace_bytes(const ssm_params_t* p);
 /* Number of floats of p->states: B * ceil(L/8) * D * N. */
 SSM_API size_t ssm_states_elems(const ssm_params_t* p);
 
 /* Forward (see top of file).  Writes out and states. */
 SSM_API int ssm_fwd(const ssm_params_t* p, ssm_stream_t stream);
 /* Backward.  Needs the states written by ssm_fwd on the same inputs.  Writes
- * du, ddelta, dA, dB, dC and, when present, dD, ddelta_bias, dz (overwritten). */
+ * du, ddelta, dA, dB, dC and, when present, dD, ddelta_bias, dz (overwritten).
+ * Every output is bit-reproducible from call to call: sums over channels (dB,
+ * dC) and over steps (dA, dD, ddelta_bias) are formed in a fixed order. */
 SSM_API int ssm_bwd(const ssm_params_t* p, ssm_stream_t stream);
 
 /* Both directions of a BidirectionalMamba block in one launch each.  fwd and
@@ -156,7 +164,9 @@ SSM_API int ssm_bwd_bidir(const ssm_params_t* fwd, const ssm_params_t* rev, ssm_
  * zeroes its own copy and all GPUs pass a cross-GPU barrier before any GPU's
  * call; after every GPU's call and a second barrier, each copy holds the full
  * sums.  p->dB and p->dC are not written (they may be NULL); everything else
- * is as in ssm_bwd.  dbc_mc must be 16-byte aligned.                        */
+ * is as in ssm_bwd.  dbc_mc must be 16-byte aligned.  p->workspace needs
+ * ssm_bwd_workspace_bytes(p, 1) bytes.  The order of the cross-GPU adds is
+ * not fixed, so these dB / dC may differ in the last bits between calls.   */
 SSM_API int ssm_bwd_bc_multicast(const ssm_params_t* p, float* dbc_mc, ssm_stream_t stream);
 
 /* ---- causal depthwise conv1d + activation (selectssm.py:167-187) ----
@@ -230,11 +240,17 @@ SSM_API const char* ssm_strerror(int status);
  * p->workspace comes from one static device array of SSM_NOALLOC_SCRATCH_BYTES
  * per GPU (held until the process exits); p->workspace is ignored and all
  * inputs and outputs are still the caller's.  Returns SSM_ERR_WORKSPACE when
- * ssm_workspace_bytes(p) exceeds the array.  The first call on each device
- * looks up the array's device address; make that call before any stream
- * capture.  Calls share the array, so calls that overlap on the GPU (other
- * streams, other host threads, same device) race; the backward re-initialises
- * every scratch byte it reads, so no state leaks between calls. */
+ * ssm_bwd_workspace_bytes(p, 0) exceeds the array.  The first call on each
+ * device looks up the array's device address and keeps it for the life of the
+ * process; make that call before any stream capture.  A device reset
+ * (cudaDeviceReset, or the primary context destroyed and re-created) makes the
+ * kept address stale: do not call this after one.  Calls share the array, so
+ * calls that overlap on the GPU (other streams, other host threads, same
+ * device) race; the backward re-initialises every scratch byte it reads, so no
+ * state leaks between calls.  This covers the backward only: the forward,
+ * ssm_fwd, still takes p->workspace when it splits a long sequence into
+ * segments or when B / C are bf16 (ssm_fwd_workspace_bytes(p) bytes; 0 means
+ * ssm_fwd needs no workspace for these params). */
 #define SSM_NOALLOC_SCRATCH_BYTES (8u << 20)
 SSM_API int ssm_bwd_noalloc(const ssm_params_t* p, ssm_stream_t stream);
 

@@ -43,7 +43,7 @@ EXPORTED_SYMBOLS = (
     "ssm_conv1d_workspace_bytes", "ssm_conv1d_act_fwd", "ssm_conv1d_act_bwd", "ssm_strerror", "ssm_last_error",
     "ssm_version", "ssm_bwd_noalloc", "ssm_launch_count",
     "ssm_rmsnorm_workspace_bytes", "ssm_rmsnorm_fwd", "ssm_rmsnorm_bwd", "ssm_selftest_wait_timeout",
-    "ssm_bwd_bc_multicast",
+    "ssm_bwd_bc_multicast", "ssm_bwd_workspace_bytes", "ssm_fwd_workspace_bytes",
 )
 
 
@@ -118,6 +118,8 @@ def load(path: str | None = None) -> ctypes.CDLL:
     sigs = {
         "ssm_workspace_bytes": (ctypes.c_size_t, [P]),
         "ssm_states_elems": (ctypes.c_size_t, [P]),
+        "ssm_bwd_workspace_bytes": (ctypes.c_size_t, [P, ctypes.c_int]),
+        "ssm_fwd_workspace_bytes": (ctypes.c_size_t, [P]),
         "ssm_fwd": (ctypes.c_int, [P, ctypes.c_void_p]),
         "ssm_bwd": (ctypes.c_int, [P, ctypes.c_void_p]),
         "ssm_fwd_bidir": (ctypes.c_int, [P, P, ctypes.c_void_p]),

@@ -48,7 +48,7 @@ static int scratch_address(void** out) {
 extern "C" SSM_API int ssm_bwd_noalloc(const ssm_params_t* p, ssm_stream_t stream) {
   using namespace ssm;
   if (!p) return SSM_ERR_NULL;
-  const size_t need = ssm_workspace_bytes(p);
+  const size_t need = ssm_bwd_workspace_bytes(p, 0);
   if (need > SSM_NOALLOC_SCRATCH_BYTES) return SSM_ERR_WORKSPACE;
   const bool empty = (int64_t)p->batch * p->seqlen * p->dim == 0;
   if (!empty || p->dA) {

@@ -45,14 +45,6 @@ int bind_device(const void* ptr) {
   } while (0)
 
 // ---------------------------------------------------------------- small kernels
-// Zeroes `rows` rows of 16 floats spaced `stride` floats apart.
-__global__ void zero_rows16_kernel(float* p, int64_t rows, int64_t stride) {
-  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;  // one float4 per thread
-  if (i >= rows * 4) return;
-  const int64_t r = i >> 2;
-  reinterpret_cast<float4*>(p + r * stride)[i & 3] = make_float4(0.f, 0.f, 0.f, 0.f);
-}
-
 // Widens the bf16 rows of B and C (16 elements, row stride `stride` elements)
 // to dense float32 rows, one 16-byte load (8 elements) per thread and tensor.
 // The scan kernels read every B / C element once per channel, so converting
@@ -101,12 +93,22 @@ __global__ void finalize_kernel(FinalizeDir f) {
       f.dbias[i] = s;
     }
   }
-  if (f.convert_bc) {
-    const int64_t nBC = (int64_t)f.batch * f.L * kN;
-    for (int64_t e = i; e < nBC; e += (int64_t)gridDim.x * blockDim.x) {
-      const int64_t r = e / kN, n = e % kN;
-      reinterpret_cast<TBC*>(f.dB)[r * f.bc_stride + n] = Cvt<TBC>::from_f(f.dB_acc[e]);
-      reinterpret_cast<TBC*>(f.dC)[r * f.bc_stride + n] = Cvt<TBC>::from_f(f.dC_acc[e]);
+  if (f.bc_part) {  // dB | dC: sum the channel tiles' partials in tile order, 4 states per thread
+    const int64_t rows = (int64_t)f.batch * f.L;
+    const float4* P = reinterpret_cast<const float4*>(f.bc_part);
+    for (int64_t e = i; e < rows * 8; e += (int64_t)gridDim.x * blockDim.x) {
+      float4 v = P[e];
+      for (int k = 1; k < f.ntile; ++k) {
+        const float4 w = P[(int64_t)k * rows * 8 + e];
+        v.x += w.x; v.y += w.y; v.z += w.z; v.w += w.w;
+      }
+      const int64_t r = e >> 3;
+      const int q = (int)(e & 7);
+      TBC* dst = reinterpret_cast<TBC*>(q < 4 ? f.dB : f.dC) + r * f.bc_stride + (q & 3) * 4;
+      dst[0] = Cvt<TBC>::from_f(v.x);
+      dst[1] = Cvt<TBC>::from_f(v.y);
+      dst[2] = Cvt<TBC>::from_f(v.z);
+      dst[3] = Cvt<TBC>::from_f(v.w);
     }
   }
 }
@@ -298,12 +300,17 @@ static size_t fwd_seg_bytes(const Geo& g) {
 
 static size_t fwd_ws_bytes(const Geo& g) { return fwd_seg_bytes(g) + wide_bc_bytes(g); }
 
-static size_t bwd_ws_bytes(const Geo& g) {
+// per-channel-tile dB | dC partials: (tiles, B, L, 32) float32
+static size_t bc_part_bytes(const Geo& g) {
+  return round256((size_t)((g.Dm + kBTile - 1) / kBTile) * g.B * g.L * 2 * kN * 4);
+}
+
+static size_t bwd_ws_bytes(const Geo& g, bool multicast = false) {
   const Seg sg = choose_segments(g, kBwdSeg);
   const size_t rows = (size_t)g.B * sg.nseg * g.Dm;
   size_t n = round256(rows * kN * 4) + 2 * round256(rows * 4);
-  if (g.bcbf16) n += 2 * round256((size_t)g.B * g.L * kN * 4);  // float32 dB / dC accumulators
   if (sg.nseg > 1) n += round256(rows * kN * 4) + round256(rows * 4);  // segF, segT
+  if (!multicast) n += bc_part_bytes(g);  // the multicast form sums dB / dC in the caller's buffer
   return n + wide_bc_bytes(g);
 }
 
@@ -421,7 +428,7 @@ static int launch_fwd(FwdLaunch& L, int ndir, const Geo& g, cudaStream_t s) {
 
 // ---------------------------------------------------------------- backward launch
 struct BwdWs {
-  float *dA_part, *dD_part, *db_part, *dB_acc, *dC_acc, *segF, *segT, *Bw, *Cw;
+  float *dA_part, *dD_part, *db_part, *bc_part, *dB_acc, *dC_acc, *segF, *segT, *Bw, *Cw;
   int64_t acc_stride;
 };
 
@@ -441,24 +448,20 @@ static void carve_ws(const ssm_params_t* p, const Geo& g, char* ws, BwdWs* w, fl
     w->segT = reinterpret_cast<float*>(ws);
     ws += round256(rows * 4);
   }
+  w->bc_part = w->dB_acc = w->dC_acc = nullptr;
+  w->acc_stride = kN;
+  if (dbc_mc) {  // the partial sums go to the caller's multicast buffer (dense rows)
+    w->dB_acc = dbc_mc;
+    w->dC_acc = dbc_mc + (size_t)g.B * g.L * kN;
+  } else {
+    w->bc_part = reinterpret_cast<float*>(ws);
+    ws += bc_part_bytes(g);
+  }
   if (g.bcbf16) {
-    w->dB_acc = reinterpret_cast<float*>(ws);
-    ws += round256((size_t)g.B * g.L * kN * 4);
-    w->dC_acc = reinterpret_cast<float*>(ws);
-    ws += round256((size_t)g.B * g.L * kN * 4);
-    w->acc_stride = kN;
     w->Bw = reinterpret_cast<float*>(ws);
     w->Cw = reinterpret_cast<float*>(ws + wide_bc_bytes(g) / 2);
   } else {
     w->Bw = w->Cw = nullptr;
-    w->dB_acc = reinterpret_cast<float*>(p->dB);
-    w->dC_acc = reinterpret_cast<float*>(p->dC);
-    w->acc_stride = g.bs;
-  }
-  if (dbc_mc) {  // the partial sums go to the caller's multicast buffer (dense rows)
-    w->dB_acc = dbc_mc;
-    w->dC_acc = dbc_mc + (size_t)g.B * g.L * kN;
-    w->acc_stride = kN;
   }
 }
 
@@ -488,6 +491,7 @@ static int fill_bwd_dir(const ssm_params_t* p, const Geo& g, const BwdWs& w, Bwd
   d->du = p->du;
   d->ddelta = p->ddelta;
   d->dz = p->dz;
+  d->bc_part = w.bc_part;
   d->dB_acc = w.dB_acc;
   d->dC_acc = w.dC_acc;
   d->bc_mode = multicast ? kBcMulticast : kBcLocal;
@@ -572,19 +576,6 @@ static int launch_bwd(BwdLaunch& L, int ndir, const Geo& g, cudaStream_t s) {
   return launch_bwd_g<float, float>(L, ndir, g, s);
 }
 
-static int launch_zero_acc(const Geo& g, const BwdWs& w, cudaStream_t s) {
-  const int64_t rows = (int64_t)g.B * g.L;
-  if (rows == 0) return SSM_OK;
-  const int64_t n = rows * 4;
-  const int threads = 256;
-  const unsigned blocks = (unsigned)((n + threads - 1) / threads);
-  zero_rows16_kernel<<<blocks, threads, 0, s>>>(w.dB_acc, rows, w.acc_stride);
-  zero_rows16_kernel<<<blocks, threads, 0, s>>>(w.dC_acc, rows, w.acc_stride);
-  note_launches(2);
-  SSM_CUDA_CHECK(cudaGetLastError(), "launch zero_rows16_kernel");
-  return SSM_OK;
-}
-
 static int launch_finalize(const ssm_params_t* p, const Geo& g, const BwdWs& w, cudaStream_t s, bool reduced) {
   FinalizeDir f;
   f.dA_part = w.dA_part;
@@ -593,20 +584,24 @@ static int launch_finalize(const ssm_params_t* p, const Geo& g, const BwdWs& w, 
   f.dA = p->dA;
   f.dD = p->D ? p->dD : nullptr;
   f.dbias = p->delta_bias ? p->ddelta_bias : nullptr;
-  f.dB_acc = w.dB_acc;
-  f.dC_acc = w.dC_acc;
+  f.bc_part = reduced ? nullptr : w.bc_part;
   f.dB = p->dB;
   f.dC = p->dC;
   f.bc_stride = g.bs;
   f.prows = g.B * choose_segments(g, kBwdSeg).nseg;
+  f.ntile = (g.Dm + kBTile - 1) / kBTile;
   f.batch = g.B;
   f.L = g.L;
   f.Dm = g.Dm;
-  f.convert_bc = g.bcbf16 && !reduced && (int64_t)g.B * g.L > 0;
   const int threads = 256;
   int64_t n = (int64_t)g.Dm * kN;
   unsigned blocks = (unsigned)((n + threads - 1) / threads);
-  if (f.convert_bc) blocks = blocks < 1184 ? 1184 : blocks;
+  if (f.bc_part) {  // enough threads for the dB / dC rows (grid-stride beyond 8 CTAs per SM)
+    const int64_t nbc = ((int64_t)g.B * g.L * 8 + threads - 1) / threads;
+    const int64_t cap = 8L * kSMs;
+    const unsigned want = (unsigned)(nbc < cap ? nbc : cap);
+    blocks = blocks < want ? want : blocks;
+  }
   if (blocks == 0) return SSM_OK;
   if (g.bcbf16)
     finalize_kernel<__nv_bfloat16><<<blocks, threads, 0, s>>>(f);
@@ -636,6 +631,19 @@ size_t ssm_workspace_bytes(const ssm_params_t* p) {
   Geo g;
   if (check_common(p, &g) != SSM_OK) return 0;
   return ws_bytes(g);
+}
+
+size_t ssm_bwd_workspace_bytes(const ssm_params_t* p, int multicast) {
+  Geo g;
+  if (check_common(p, &g) != SSM_OK) return 0;
+  return bwd_ws_bytes(g, multicast != 0);
+}
+
+size_t ssm_fwd_workspace_bytes(const ssm_params_t* p) {
+  Geo g;
+  if (check_common(p, &g) != SSM_OK) return 0;
+  if ((int64_t)g.B * g.L * g.Dm == 0) return 0;
+  return fwd_ws_bytes(g);
 }
 
 int ssm_fwd(const ssm_params_t* p, ssm_stream_t stream) { return ssm_fwd_bidir(p, nullptr, stream); }
@@ -682,12 +690,12 @@ static int bwd_impl(const ssm_params_t* fwd, const ssm_params_t* rev, float* dbc
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   st = bind_device((int64_t)g.B * g.L * g.Dm ? fwd->u : (const void*)fwd->dA);
   if (st) return st;
-  const size_t need = bwd_ws_bytes(g) * (rev ? 2 : 1);
+  const size_t need = bwd_ws_bytes(g, dbc_mc != nullptr) * (rev ? 2 : 1);
   if (need && (!fwd->workspace || fwd->workspace_bytes < need)) return SSM_ERR_WORKSPACE;
   if (reinterpret_cast<uintptr_t>(fwd->workspace) & 255u) return SSM_ERR_ALIGN;
   BwdWs w[2];
   carve_ws(fwd, g, static_cast<char*>(fwd->workspace), &w[0], dbc_mc);
-  if (rev) carve_ws(rev, g, static_cast<char*>(fwd->workspace) + bwd_ws_bytes(g), &w[1], dbc_mc);
+  if (rev) carve_ws(rev, g, static_cast<char*>(fwd->workspace) + bwd_ws_bytes(g, dbc_mc != nullptr), &w[1], dbc_mc);
   const int ndir = rev ? 2 : 1;
   const ssm_params_t* ps[2] = {fwd, rev};
   if ((int64_t)g.B * g.L * g.Dm == 0) {
@@ -706,10 +714,6 @@ static int bwd_impl(const ssm_params_t* fwd, const ssm_params_t* rev, float* dbc
   for (int d = 0; d < ndir; ++d) {
     st = fill_bwd_dir(ps[d], g, w[d], &args.dir[d], s, dbc_mc != nullptr);
     if (st) return st;
-    if (!dbc_mc) {  // the multicast buffer is zeroed by its owners
-      st = launch_zero_acc(g, w[d], s);
-      if (st) return st;
-    }
   }
   st = launch_bwd(args, ndir, g, s);
   if (st) return st;

@@ -21,8 +21,9 @@
 //   32 channels.  Lanes hold their 4 state quads in an order permuted by lane
 //   bits 4 and 3 (A, B, C, the restart state and dA are read/written at the
 //   permuted addresses), so the first two exchange stages need no selects.
-//   The 4 warps' partials are summed in shared memory and added over channel
-//   tiles with 16-byte atomics.  dA/dD/d(delta_bias) are per-(batch row,
+//   The 4 warps' partials are summed in shared memory and stored as this
+//   channel tile's partial; the finalize kernel sums the tiles in a fixed
+//   order, so dB / dC are bit-reproducible.  dA/dD/d(delta_bias) are per-(batch row,
 //   segment) partials summed in a fixed order by the finalize kernel.
 //   The gate activation is a template parameter (fixed per launch) and the
 //   per-step work holds no data- or flag-dependent branch (only stores are
@@ -402,11 +403,12 @@ __global__ void __launch_bounds__(kBThreads, 2) ssm_bwd_kernel(const __grid_cons
         v.x += p.x; v.y += p.y; v.z += p.z; v.w += p.w;
       }
       if (t < L) {
-        float* dst = (q4 < 4 ? a.dB_acc : a.dC_acc) + ((size_t)b * L + t) * a.acc_stride + (q4 & 3) * 4;
-        if constexpr (MC)
-          multimem_red_add4(dst, v);  // the sum over GPUs, done in the NVSwitch
-        else
-          atomicAdd(reinterpret_cast<float4*>(dst), v);
+        if constexpr (MC) {  // the sum over GPUs, done in the NVSwitch
+          float* dst = (q4 < 4 ? a.dB_acc : a.dC_acc) + ((size_t)b * L + t) * a.acc_stride + (q4 & 3) * 4;
+          multimem_red_add4(dst, v);
+        } else {  // this tile's partial; finalize sums the tiles in order
+          *reinterpret_cast<float4*>(a.bc_part + (((size_t)blockIdx.x * gridDim.y + b) * L + t) * 32 + q4 * 4) = v;
+        }
       }
     }
   }

@@ -45,7 +45,8 @@ struct BwdDir {
   void* du;
   void* ddelta;
   void* dz;
-  float* dB_acc;   // fp32 accumulation target for dB (row stride acc_stride)
+  float* bc_part;  // (channel tiles, B, L, 32) per-tile dB | dC partial sums (kBcLocal)
+  float* dB_acc;   // kBcMulticast: NVLink multicast addresses of the dB / dC sums (row stride acc_stride)
   float* dC_acc;
   int bc_mode;     // kBcLocal / kBcMulticast
   float* dA_part;  // (B, nseg, D, 16)
@@ -58,8 +59,8 @@ struct BwdDir {
   int L, Dm, flags, gate_act, has_z;
   int nseg, seg_chunks;
 };
-// How the backward accumulates its dB / dC partial sums.
-constexpr int kBcLocal = 0;      // red.add into this GPU's dB_acc / dC_acc
+// How the backward delivers its dB / dC partial sums (sums over a CTA's channels).
+constexpr int kBcLocal = 0;      // plain stores into bc_part, summed over tiles in a fixed order by finalize
 constexpr int kBcMulticast = 1;  // multimem.red at dB_acc / dC_acc (NVLink multicast addresses)
 
 struct BwdLaunch {
@@ -108,8 +109,9 @@ __global__ void ssm_bwd_fold_kernel(const __grid_constant__ BwdLaunch P) {
   }
 }
 
-// Sums the per-batch-row partials in batch order (deterministic) and converts
-// the fp32 dB/dC accumulators when B/C are bf16.
+// Sums the per-(batch row, segment) partials of dA / dD / d(bias) in row order
+// and the per-channel-tile dB / dC partials in tile order (both deterministic),
+// writing dB / dC in the caller's dtype and row stride.
 struct FinalizeDir {
   const float* dA_part;
   const float* dD_part;
@@ -117,13 +119,13 @@ struct FinalizeDir {
   float* dA;
   float* dD;
   float* dbias;
-  const float* dB_acc;
-  const float* dC_acc;
+  const float* bc_part;  // (ntile, batch, L, 32) or null (dB / dC delivered elsewhere)
   void* dB;
   void* dC;
   int64_t bc_stride;
   int prows;  // rows of partials (batch x segments)
-  int batch, L, Dm, convert_bc;
+  int ntile;  // channel tiles of the backward
+  int batch, L, Dm;
 };
 
 }  // namespace ssm

@@ -189,9 +189,16 @@ class _Prepared:
         return g
 
 
-def _workspace(p: _lib.SSMParams, device, extra=None) -> torch.Tensor:
+def _workspace(p: _lib.SSMParams, device, extra=None, kind=None) -> torch.Tensor:
+    """Scratch for one call: ``kind`` "fwd", "bwd" or "bwd_mc" sizes it for
+    that call alone; None for any call on these params (and ``extra``)."""
     lib = _lib.load()
-    n = lib.ssm_workspace_bytes(p) + (0 if extra is None else lib.ssm_workspace_bytes(extra))
+    if kind == "fwd":
+        n = lib.ssm_fwd_workspace_bytes(p)
+    elif kind in ("bwd", "bwd_mc"):
+        n = lib.ssm_bwd_workspace_bytes(p, int(kind == "bwd_mc"))
+    else:
+        n = lib.ssm_workspace_bytes(p) + (0 if extra is None else lib.ssm_workspace_bytes(extra))
     ws = torch.empty(max(n, 256), dtype=torch.uint8, device=device)
     p.workspace, p.workspace_bytes = ws.data_ptr(), ws.numel()
     return ws
@@ -207,7 +214,7 @@ class _SelectiveScanFn(torch.autograd.Function):
         out = torch.empty(pr.shape, dtype=pr.dtype, device=pr.u.device)
         states = pr.new_states()
         p = pr.params(out=out, out_stride=pr.shape[2], states=states)
-        ws = _workspace(p, pr.u.device)  # segment carries (long sequences, few channels)
+        ws = _workspace(p, pr.u.device, kind="fwd")  # segment carries, widened bf16 B / C
         _lib.check(_lib.load().ssm_fwd(ctypes_byref(p), _stream()), "ssm_fwd")
         del ws
         ctx.pr = pr
@@ -223,7 +230,7 @@ class _SelectiveScanFn(torch.autograd.Function):
         dout = _dense(dout.to(pr.dtype))
         p = pr.params(states=states)
         g = pr.grads(p, dout, pr.shape[2])
-        ws = _workspace(p, pr.u.device)
+        ws = _workspace(p, pr.u.device, kind="bwd" if ctx.bc_sum is None else "bwd_mc")
         if ctx.bc_sum is None:
             _lib.check(_lib.load().ssm_bwd(ctypes_byref(p), _stream()), "ssm_bwd")
         else:  # dB / dC summed over the channel shards inside the kernel
