@@ -536,7 +536,7 @@ static int launch_bwd_t(BwdLaunch& L, int ndir, const Geo& g, cudaStream_t s) {
                    "cudaFuncSetAttribute(ssm_bwd_agg_kernel)");
     L.zdiv = nseg - 1;
     grid.z = ndir * (nseg - 1);
-    agg<<<grid, kBThreads, abytes, s>>>(L);
+    agg<<<grid, kAggThreads, abytes, s>>>(L);
     note_launches(1);
   SSM_CUDA_CHECK(cudaGetLastError(), "launch ssm_bwd_agg_kernel");
     dim3 fgrid((g.Dm * kN + 255) / 256, ndir, g.B);

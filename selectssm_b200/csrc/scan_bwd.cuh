@@ -2,28 +2,35 @@
 //
 // Work decomposition
 //   CTA   = one batch row b x 128 consecutive channels x one sequence segment;
-//           4 warps, lane = channel, so every lane owns all 16 states of its
-//           channel (packed f32x2 pairs).  Per-step scalars (softplus(dt),
-//           dt*x, the gated upstream gradient) and the sums over states
-//           (y, dx, ddt) are lane-local: no shuffles over states.
+//           8 warps of 16 channels.  A channel belongs to two lanes of its
+//           warp (lane = 16 hs + channel), each owning 8 of the 16 states
+//           (hs = 0: states 0-7, hs = 1: states 8-15) as 4 packed f32x2 pairs,
+//           so a thread holds half the state of a lane-per-channel layout and
+//           twice as many warps fit on an SM (16, at most 128 registers).
 //   time  = TMA stages of 16 steps (u, delta, dout, z tiles of 128 ch x 16
 //           steps; B and C tiles of 16 x 16), double buffered on mbarriers and
 //           visited last to first; each stage is two 8-step blocks, last first.
-//   block = restart from the state the forward saved before the block (plain
-//           128-bit loads), recompute alpha_t = exp(A dt_t) and alpha_t h_{t-1}
-//           for the 8 steps into tensor memory (TMEM: 8 steps x 32 values = 256
-//           columns per lane, 2 CTAs per SM), then run the adjoint
+//   block = per-step scalars first: the two lanes of a channel each evaluate
+//           softplus(dt), dt*x and the gated upstream gradient for one step of
+//           every step pair and swap them (one shuffle each), so the scalar work
+//           is not duplicated.  Then restart from the state the forward saved
+//           before the block (plain 128-bit loads), recompute alpha_t = exp(A dt_t)
+//           and alpha_t h_{t-1} for the 8 steps into tensor memory (TMEM: 8 steps
+//           x 16 values = 128 columns per lane; warps 0-3 and 4-7 share the 128
+//           TMEM lanes and use column halves), then run the adjoint
 //           f_t = alpha_{t+1} f_{t+1} + C_t dy_t backwards reading them back.
+//           Sums over states (y, sum_n f B, sum_n f A alpha h) add the two
+//           halves with one shuffle; each lane then finishes the per-step
+//           epilogue (du, ddelta, dz stores) of its own step of every pair.
 //   Leaf gradients (src/selectssm/ssmrecscan.py:150-161):
 //     dx_t = dt_t sum_n f B_t,  dA += dt_t f alpha_t h_{t-1},  dB_t = sum_d dt_t x_t f,
 //     dC_t = sum_d dy_t h_t,    ddt_t = sum_n f (A alpha_t h_{t-1} + B_t x_t).
-//   dB / dC (sums over channels) use a shuffle reduce-scatter over the warp's
-//   32 channels.  Lanes hold their 4 state quads in an order permuted by lane
-//   bits 4 and 3 (A, B, C, the restart state and dA are read/written at the
-//   permuted addresses), so the first two exchange stages need no selects.
-//   The 4 warps' partials are summed in shared memory and stored as this
-//   channel tile's partial; the finalize kernel sums the tiles in a fixed
-//   order, so dB / dC are bit-reproducible.  dA/dD/d(delta_bias) are per-(batch row,
+//   dB / dC (sums over channels) use a shuffle reduce-scatter over the 16
+//   channels of a half-warp.  Lanes hold their two state quads in an order
+//   swapped by lane bit 3, so the first exchange needs no selects.  The 8
+//   warps' partials are summed in shared memory and stored as this channel
+//   tile's partial; the finalize kernel sums the tiles in a fixed order, so
+//   dB / dC are bit-reproducible.  dA/dD/d(delta_bias) are per-(batch row,
 //   segment) partials summed in a fixed order by the finalize kernel.
 //   The gate activation is a template parameter (fixed per launch) and the
 //   per-step work holds no data- or flag-dependent branch (only stores are
@@ -40,10 +47,11 @@
 namespace ssm {
 
 constexpr int kBTile = 128;                            // channels per backward CTA
-constexpr int kBWarps = kBTile / 32;
-constexpr int kBThreads = kBTile;
+constexpr int kBWarps = kBTile / 16;                   // 16 channels per warp
+constexpr int kBThreads = 2 * kBTile;
 constexpr int kBStages = 2;
-constexpr uint32_t kBTmemCols = kCk * 2 * kN;          // 8 steps x (16 alpha + 16 alpha*h)
+constexpr uint32_t kBTmemCols = 2 * kCk * kN;          // 2 warp groups x 8 steps x (8 alpha + 8 alpha*h)
+constexpr int kAggThreads = kBTile;                    // pre-pass: one lane per channel
 
 // Shared-memory layout (bytes), sized at run time: the output-frame copy of u
 // and the scan-frame copies of dout / z only exist for the reverse direction
@@ -75,18 +83,16 @@ struct BwdLayout {
   }
 };
 
-// Sum over the 32 channel-lanes of a warp of a lane's 16 per-state values
-// (8 packed pairs).  Pair slot p holds states 4 (q ^ xq) + 2 (p & 1) + {0, 1},
-// q = p >> 1, with xq = (lane bit 4) << 1 | (lane bit 3).  The result is the
-// total for state 4 xq + 2 (lane bit 2) + (lane bit 1).
-__device__ __forceinline__ float reduce32ch(const float2 (&v)[8], bool b2, bool b1) {
-  float2 r[4];
+// Sum over the 16 channel-lanes of a half-warp of a lane's 8 per-state values
+// (4 packed pairs).  Pair slot p holds states 8 hs + 4 ((p >> 1) ^ b3) +
+// 2 (p & 1) + {0, 1} (b3 = lane bit 3).  The result is the total for state
+// 8 hs + 4 b3 + 2 b2 + b1 (lane bits 2 and 1); lanes differing in bit 0 hold
+// the same total.
+__device__ __forceinline__ float reduce16ch(const float2 (&v)[4], bool b2, bool b1) {
+  float2 r[2];
 #pragma unroll
-  for (int p = 0; p < 4; ++p)  // lane bit 4: keep quads 0,1, receive the partner's quads 2,3
-    r[p] = fadd2(v[p], make_float2(__shfl_xor_sync(kFull, v[p + 4].x, 16), __shfl_xor_sync(kFull, v[p + 4].y, 16)));
-#pragma unroll
-  for (int p = 0; p < 2; ++p)  // lane bit 3: keep quad 0
-    r[p] = fadd2(r[p], make_float2(__shfl_xor_sync(kFull, r[p + 2].x, 8), __shfl_xor_sync(kFull, r[p + 2].y, 8)));
+  for (int p = 0; p < 2; ++p)  // lane bit 3: keep quad slot 0, receive the partner's quad slot 1
+    r[p] = fadd2(v[p], make_float2(__shfl_xor_sync(kFull, v[p + 2].x, 8), __shfl_xor_sync(kFull, v[p + 2].y, 8)));
   // lane bit 2: keep one pair of the quad
   const float2 kp = b2 ? r[1] : r[0], sd = b2 ? r[0] : r[1];
   const float2 s = fadd2(kp, make_float2(__shfl_xor_sync(kFull, sd.x, 4), __shfl_xor_sync(kFull, sd.y, 4)));
@@ -96,43 +102,39 @@ __device__ __forceinline__ float reduce32ch(const float2 (&v)[8], bool b2, bool 
   return q;
 }
 
-// 16 per-state values at permuted quad addresses -> 8 pairs
+// This lane's 8 per-state values (states 8 hs .. 8 hs + 7, quads swapped by
+// lane bit 3) -> 4 pairs.  `row` points at state 0 of a 16-state row; `q0` is
+// the offset of quad slot 0 (8 hs + 4 b3), slot 1 is at q0 ^ 4.
 template <typename TB>
-__device__ __forceinline__ void ld16q(const TB* row, int xq, float2 (&v)[8]) {
+__device__ __forceinline__ void ld8q(const TB* row, int q0, float2 (&v)[4]) {
+  const float4 f0 = ld4(row + q0), f1 = ld4(row + (q0 ^ 4));
+  v[0] = make_float2(f0.x, f0.y);
+  v[1] = make_float2(f0.z, f0.w);
+  v[2] = make_float2(f1.x, f1.y);
+  v[3] = make_float2(f1.z, f1.w);
+}
+
+// 16 per-state values in natural order -> 8 pairs
+template <typename TB>
+__device__ __forceinline__ void ld16(const TB* row, float2 (&v)[8]) {
 #pragma unroll
   for (int q = 0; q < 4; ++q) {
-    const float4 f = ld4(row + 4 * (q ^ xq));
+    const float4 f = ld4(row + 4 * q);
     v[2 * q] = make_float2(f.x, f.y);
     v[2 * q + 1] = make_float2(f.z, f.w);
   }
 }
 
-__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const float (&v)[16]) {
   asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
-      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+          taddr),
       "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
       "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
       "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])),
       "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
       "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
-      "r"(__float_as_uint(v[15])), "r"(__float_as_uint(v[16])), "r"(__float_as_uint(v[17])),
-      "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])), "r"(__float_as_uint(v[20])),
-      "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])), "r"(__float_as_uint(v[23])),
-      "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])), "r"(__float_as_uint(v[26])),
-      "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])),
-      "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
-      : "memory");
-}
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr)
+      "r"(__float_as_uint(v[15]))
       : "memory");
 }
 
@@ -149,7 +151,8 @@ __global__ void __launch_bounds__(kBThreads, 2) ssm_bwd_kernel(const __grid_cons
   const int b = blockIdx.y;
   const int c0 = blockIdx.x * kBTile;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int cl = threadIdx.x;  // channel within the tile
+  const int hs = lane >> 4;                   // state half of this lane
+  const int cl = warp * 16 + (lane & 15);     // channel within the tile
   const int c = c0 + cl;
   const int L = a.L, Dm = a.Dm;
   if (c0 >= Dm) return;
@@ -181,7 +184,8 @@ __global__ void __launch_bounds__(kBThreads, 2) ssm_bwd_kernel(const __grid_cons
   __syncthreads();
   tmem_fence_after_sync();
   const uint32_t tbase = *tmem_slot;
-  const uint32_t trow = tbase + ((uint32_t)(warp * 32) << 16);  // this warp's lane quarter
+  // this warp's lane quarter and column half
+  const uint32_t trow = tbase + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)((warp >> 2) * kCk * kN);
 
   const uint32_t tx = BwdLayout::tx(sizeof(T), sizeof(TBC), has_z, mirror);
   auto issue = [&](int it) {  // it-th load is chunk j1-1-it (last first)
@@ -208,25 +212,28 @@ __global__ void __launch_bounds__(kBThreads, 2) ssm_bwd_kernel(const __grid_cons
     for (int it = 0; it < npre; ++it) issue(it);
   }
 
-  // state permutation (see reduce32ch)
-  const int xq = (((lane >> 4) & 1) << 1) | ((lane >> 3) & 1);
-  const bool b2 = ((lane >> 2) & 1) != 0, b1 = ((lane >> 1) & 1) != 0;
-  const int red_n = 4 * xq + (b2 ? 2 : 0) + (b1 ? 1 : 0);
+  // state layout (see reduce16ch / ld8q)
+  const bool b3 = ((lane >> 3) & 1) != 0, b2 = ((lane >> 2) & 1) != 0, b1 = ((lane >> 1) & 1) != 0;
+  const int q0 = 8 * hs + (b3 ? 4 : 0);
+  const int red_n = q0 + (b2 ? 2 : 0) + (b1 ? 1 : 0);
   const bool red_writer = (lane & 1) == 0;
-  // A (pairs at the permuted quad addresses) is re-read from L1 at each use
-  // rather than held in 16 registers.
-  const float* Arow = a.A + (size_t)(cvalid ? c : 0) * kN;
-  auto An_at = [&](int p) {
-    return __ldg(reinterpret_cast<const float2*>(Arow + 4 * ((p >> 1) ^ xq) + 2 * (p & 1)));
-  };
+  const bool own_odd = hs != 0;  // this lane finishes the odd step of every step pair
+  float2 A2[4];  // A log2(e), this lane's states
+  {
+    float2 Av[4];
+    const float* Arow = a.A + (size_t)(cvalid ? c : 0) * kN;
+    ld8q(Arow, q0, Av);
+#pragma unroll
+    for (int p = 0; p < 4; ++p) A2[p] = fmul2(Av[p], dup2(kLog2e));
+  }
   const float bias = (a.bias && cvalid) ? a.bias[c] : 0.f;
   const float Dsc = (has_D && cvalid) ? a.D[c] : 0.f;                  // skip weight, scan channel
   const float Dso = (has_D && cvalid) ? a.D[aligned ? c : co] : 0.f;   // skip weight in the pre-gate value
-  float2 fa[8], dA[8];  // f_{t+1} alpha_{t+1} carried backwards; dA accumulators
+  float2 fa[4], dA[4];  // f_{t+1} alpha_{t+1} carried backwards; dA accumulators (A log2 e frame)
 #pragma unroll
-  for (int p = 0; p < 8; ++p) fa[p] = dA[p] = make_float2(0.f, 0.f);
+  for (int p = 0; p < 4; ++p) fa[p] = dA[p] = make_float2(0.f, 0.f);
   if (a.nseg > 1 && cvalid)  // adjoint entering this segment from the later ones
-    ld16q(a.segF + (((size_t)b * a.nseg + seg) * Dm + c) * kN, xq, fa);
+    ld8q(a.segF + (((size_t)b * a.nseg + seg) * Dm + c) * kN, q0, fa);
   float dD_acc = 0.f, db_acc = 0.f;
   T* du_g = reinterpret_cast<T*>(a.du) + (size_t)b * L * Dm + c;
   T* dd_g = reinterpret_cast<T*>(a.ddelta) + (size_t)b * L * Dm + c;
@@ -258,62 +265,74 @@ __global__ void __launch_bounds__(kBThreads, 2) ssm_bwd_kernel(const __grid_cons
     for (int blk = 1; blk >= 0; --blk) {
       const int T0 = blk * kCk;
       const int ck = j * (kChunk / kCk) + blk;  // global 8-step block index
-      // ---- per-step scalars of the block (own channel)
-      // (sgv: upstream gradient of the skip term in the scan frame; it differs
-      // from dyv only for the reference's reverse-skip frame)
-      // (zgv: act'(z) of the step, for dz; spv: d softplus / d delta, for ddelta)
-      float dtv[kCk], dxv[kCk], dyv[kCk], sgv[kCk], zgv[kCk], spv[kCk];
+      // ---- per-step scalars: this lane evaluates step 2k + hs of each pair k
+      // (own step) and receives the partner's step with one shuffle each.
+      // (sgo: upstream gradient of the skip term in the scan frame; it differs
+      // from dy only for the reference's reverse-skip frame; zgo: act'(z);
+      // spo: d softplus / d delta)
+      float dtv[kCk], dxv[kCk], dyv[kCk];
+      float dto[kCk / 2], sgo[kCk / 2], zgo[kCk / 2], spo[kCk / 2];
 #pragma unroll
-      for (int u = 0; u < kCk; ++u) {
-        const int tl = T0 + u;
+      for (int k = 0; k < kCk / 2; ++k) {
+        const int tl = T0 + 2 * k + hs;
         const bool valid = j * kChunk + tl < L;
         const float x = ld_f(su + tl * kBTile);
         const float dr = ld_f(sd + tl * kBTile) + bias;
-        spv[u] = 1.f;
-        const float dt = softplus ? softplus_sig(dr, spv[u]) : dr;
-        dtv[u] = valid ? dt : 0.f;
-        dxv[u] = valid ? dt * x : 0.f;
+        float sp = 1.f;
+        float dt = softplus ? softplus_sig(dr, sp) : dr;
+        dt = valid ? dt : 0.f;
+        const float dx = valid ? dt * x : 0.f;
         const int row = rev ? kChunk - 1 - tl : tl;
         float g = ld_f(sdo + row * kBTile);
-        zgv[u] = 1.f;
+        float zg = 1.f;
         if (has_z) {
           float av;
-          act_and_grad(ld_f(szo + row * kBTile), G, av, zgv[u]);
+          act_and_grad(ld_f(szo + row * kBTile), G, av, zg);
           g *= av;
         }
-        dyv[u] = valid ? g : 0.f;
-        sgv[u] = dyv[u];
-      }
-      if (mirror) {
-#pragma unroll
-        for (int u = 0; u < kCk; ++u) {
-          const int tl = T0 + u;
-          float sg = ld_f(sds + tl * kBTile);
+        const float dy = valid ? g : 0.f;
+        float sg = dy;
+        if (mirror) {
+          sg = ld_f(sds + tl * kBTile);
           if (has_z) sg *= act_f(ld_f(szs + tl * kBTile), G);
-          sgv[u] = j * kChunk + tl < L ? sg : 0.f;
+          sg = valid ? sg : 0.f;
         }
+        dto[k] = dt;
+        sgo[k] = sg;
+        zgo[k] = zg;
+        spo[k] = sp;
+        const float pdt = __shfl_xor_sync(kFull, dt, 16);
+        const float pdx = __shfl_xor_sync(kFull, dx, 16);
+        const float pdy = __shfl_xor_sync(kFull, dy, 16);
+        dtv[2 * k] = own_odd ? pdt : dt;
+        dtv[2 * k + 1] = own_odd ? dt : pdt;
+        dxv[2 * k] = own_odd ? pdx : dx;
+        dxv[2 * k + 1] = own_odd ? dx : pdx;
+        dyv[2 * k] = own_odd ? pdy : dy;
+        dyv[2 * k + 1] = own_odd ? dy : pdy;
       }
       // ---- restart state (the forward's checkpoint before this block)
-      float2 h[8];
+      float2 h[4];
       if (ck > 0 && cvalid) {
-        ld16q(st_b + (size_t)(ck - 1) * Dm * kN, xq, h);
+        ld8q(st_b + (size_t)(ck - 1) * Dm * kN, q0, h);
       } else {
 #pragma unroll
-        for (int p = 0; p < 8; ++p) h[p] = make_float2(0.f, 0.f);
+        for (int p = 0; p < 4; ++p) h[p] = make_float2(0.f, 0.f);
       }
       // ---- forward recompute: alpha, alpha*h to TMEM; y (for dz) and dC partials
+      float yo[kCk / 2];  // y of this lane's own steps
 #pragma unroll
       for (int u = 0; u < kCk; ++u) {
         const int tl = T0 + u;
-        float2 Bq[8], Cq[8];
-        ld16q(sB + tl * kN, xq, Bq);
-        ld16q(sC + tl * kN, xq, Cq);
-        const float2 dt2 = dup2(dtv[u] * kLog2e), dx2 = dup2(dxv[u]), dy2 = dup2(dyv[u]);
-        float keep[32];
-        float2 y2 = make_float2(0.f, 0.f), vc[8];
+        float2 Bq[4], Cq[4];
+        ld8q(sB + tl * kN, q0, Bq);
+        ld8q(sC + tl * kN, q0, Cq);
+        const float2 dt2 = dup2(dtv[u]), dx2 = dup2(dxv[u]), dy2 = dup2(dyv[u]);
+        float keep[16];
+        float2 y2 = make_float2(0.f, 0.f), vc[4];
 #pragma unroll
-        for (int p = 0; p < 8; ++p) {
-          const float2 e = fmul2(An_at(p), dt2);
+        for (int p = 0; p < 4; ++p) {
+          const float2 e = fmul2(A2[p], dt2);
           const float2 al = make_float2(ex2(e.x), ex2(e.y));
           const float2 q = fmul2(al, h[p]);
           h[p] = ffma2(Bq[p], dx2, q);
@@ -321,69 +340,85 @@ __global__ void __launch_bounds__(kBThreads, 2) ssm_bwd_kernel(const __grid_cons
           vc[p] = fmul2(dy2, h[p]);
           keep[2 * p] = al.x;
           keep[2 * p + 1] = al.y;
-          keep[16 + 2 * p] = q.x;
-          keep[16 + 2 * p + 1] = q.y;
+          keep[8 + 2 * p] = q.x;
+          keep[8 + 2 * p + 1] = q.y;
         }
-        tmem_st32(trow + u * 32, keep);
-        const float dc = reduce32ch(vc, b2, b1);
+        tmem_st16(trow + u * 16, keep);
+        const float dc = reduce16ch(vc, b2, b1);
         if (red_writer) red[(warp * kChunk + tl) * 32 + kN + red_n] = dc;
-        // dz needs the pre-gate output of this step
-        if (has_z) {  // straight-line; only the store is predicated
-          const int t = j * kChunk + tl;
-          const int row = rev ? kChunk - 1 - tl : tl;
-          const int l = rev ? L - 1 - t : t;
-          const float xs = ld_f(mirror ? suo + row * kBTile : su + tl * kBTile);
-          const float pre = fmaf(Dso, xs, y2.x + y2.y);  // Dso is 0 without a skip
-          const float g = ld_f(sdo + row * kBTile) * pre * zgv[u];
-          if (t < L && cvalid) st_act(dz_g + (size_t)l * a.z_stride, g);
-        }
+        float y = y2.x + y2.y;
+        y += __shfl_xor_sync(kFull, y, 16);
+        if (u & 1) yo[u >> 1] = own_odd ? y : yo[u >> 1];
+        else yo[u >> 1] = y;
       }
       tmem_wait_st();
 
       // ---- adjoint sweep (TMEM reads double buffered one step ahead)
-      uint32_t buf[2][32];
-      tmem_ld32(trow + (kCk - 1) * 32, buf[(kCk - 1) & 1]);
+      float sbfo[kCk / 2], sawo[kCk / 2];
+      uint32_t buf[2][16];
+      tmem_ld16(trow + (kCk - 1) * 16, buf[(kCk - 1) & 1]);
       tmem_wait_ld();
 #pragma unroll
       for (int u = kCk - 1; u >= 0; --u) {
         const int tl = T0 + u;
-        if (u > 0) tmem_ld32(trow + (u - 1) * 32, buf[(u - 1) & 1]);
-        float2 Bq[8], Cq[8];
-        ld16q(sB + tl * kN, xq, Bq);
-        ld16q(sC + tl * kN, xq, Cq);
+        if (u > 0) tmem_ld16(trow + (u - 1) * 16, buf[(u - 1) & 1]);
+        float2 Bq[4], Cq[4];
+        ld8q(sB + tl * kN, q0, Bq);
+        ld8q(sC + tl * kN, q0, Cq);
         const float2 dt2 = dup2(dtv[u]), dx2 = dup2(dxv[u]), dy2 = dup2(dyv[u]);
-        float2 sAw = make_float2(0.f, 0.f), sBf = make_float2(0.f, 0.f), vb[8];
+        float2 sAw = make_float2(0.f, 0.f), sBf = make_float2(0.f, 0.f), vb[4];
 #pragma unroll
-        for (int p = 0; p < 8; ++p) {
+        for (int p = 0; p < 4; ++p) {
           const float2 al = make_float2(__uint_as_float(buf[u & 1][2 * p]), __uint_as_float(buf[u & 1][2 * p + 1]));
           const float2 q =
-              make_float2(__uint_as_float(buf[u & 1][16 + 2 * p]), __uint_as_float(buf[u & 1][16 + 2 * p + 1]));
+              make_float2(__uint_as_float(buf[u & 1][8 + 2 * p]), __uint_as_float(buf[u & 1][8 + 2 * p + 1]));
           const float2 f = ffma2(Cq[p], dy2, fa[p]);
           const float2 w = fmul2(f, q);
           dA[p] = ffma2(dt2, w, dA[p]);
-          sAw = ffma2(An_at(p), w, sAw);
+          sAw = ffma2(A2[p], w, sAw);
           sBf = ffma2(Bq[p], f, sBf);
           vb[p] = fmul2(dx2, f);
           fa[p] = fmul2(f, al);
         }
-        const float sbf = sBf.x + sBf.y, saw = sAw.x + sAw.y;
-        const float db = reduce32ch(vb, b2, b1);
+        const float db = reduce16ch(vb, b2, b1);
         if (red_writer) red[(warp * kChunk + tl) * 32 + red_n] = db;
-        // du, ddelta and the skip gradients of this step
-        // straight-line (steps past L and lanes past Dm hold zeros); only the
-        // stores are predicated
+        float sbf = sBf.x + sBf.y, saw = sAw.x + sAw.y;
+        sbf += __shfl_xor_sync(kFull, sbf, 16);
+        saw += __shfl_xor_sync(kFull, saw, 16);
+        if (u & 1) {  // the sweep visits the odd step of a pair first
+          sbfo[u >> 1] = sbf;
+          sawo[u >> 1] = saw;
+        } else {
+          sbfo[u >> 1] = own_odd ? sbfo[u >> 1] : sbf;
+          sawo[u >> 1] = own_odd ? sawo[u >> 1] : saw;
+        }
+        if (u > 0) tmem_wait_ld();
+      }
+      // ---- epilogue of this lane's own steps: du, ddelta, dz and the skip
+      // gradients (straight-line; steps past L and lanes past Dm hold zeros,
+      // only the stores are predicated)
+#pragma unroll
+      for (int k = 0; k < kCk / 2; ++k) {
+        const int tl = T0 + 2 * k + hs;
         const int t = j * kChunk + tl;
         const float x = ld_f(su + tl * kBTile);
-        const float du = fmaf(Dsc, sgv[u], dtv[u] * sbf);  // Dsc is 0 without a skip
-        dD_acc = fmaf(sgv[u], x, dD_acc);
-        float g = fmaf(x, sbf, saw);  // d/d dt
-        g *= spv[u];
+        const float du = fmaf(Dsc, sgo[k], dto[k] * sbfo[k]);  // Dsc is 0 without a skip
+        dD_acc = fmaf(sgo[k], x, dD_acc);
+        const float g = fmaf(x, sbfo[k], sawo[k] * kLn2) * spo[k];  // d/d dt (A carried as A log2 e)
         db_acc += g;
-        if (t < L && cvalid) {
+        const bool st_ok = t < L && cvalid;
+        if (st_ok) {
           st_act(du_g + (size_t)t * Dm, du);
           st_act(dd_g + (size_t)t * Dm, g);
         }
-        if (u > 0) tmem_wait_ld();
+        if (has_z) {  // dz needs the pre-gate output of the step
+          const int row = rev ? kChunk - 1 - tl : tl;
+          const int l = rev ? L - 1 - t : t;
+          const float xs = mirror ? ld_f(suo + row * kBTile) : x;
+          const float pre = fmaf(Dso, xs, yo[k]);  // Dso is 0 without a skip
+          const float gz = ld_f(sdo + row * kBTile) * pre * zgo[k];
+          if (st_ok) st_act(dz_g + (size_t)l * a.z_stride, gz);
+        }
       }
     }
 
@@ -392,8 +427,8 @@ __global__ void __launch_bounds__(kBThreads, 2) ssm_bwd_kernel(const __grid_cons
       fence_proxy_async_smem();
       issue(it + kBStages);
     }
-    {
-      // sum the 4 warps' partials: thread -> (step, 4 consecutive outputs)
+    if (threadIdx.x < kChunk * 8) {
+      // sum the 8 warps' partials: thread -> (step, 4 consecutive outputs)
       const int tl = threadIdx.x >> 3, q4 = threadIdx.x & 7;
       const int t = j * kChunk + tl;
       float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -422,15 +457,17 @@ __global__ void __launch_bounds__(kBThreads, 2) ssm_bwd_kernel(const __grid_cons
     if (threadIdx.x == 0) report(a.status, kStatusTimeout);
     return;
   }
+  dD_acc += __shfl_xor_sync(kFull, dD_acc, 16);
+  db_acc += __shfl_xor_sync(kFull, db_acc, 16);
   if (cvalid) {
     const size_t r = (size_t)b * a.nseg + seg;
     float* dAp = a.dA_part + (r * Dm + c) * kN;
-#pragma unroll
-    for (int q = 0; q < 4; ++q)
-      *reinterpret_cast<float4*>(dAp + 4 * (q ^ xq)) =
-          make_float4(dA[2 * q].x, dA[2 * q].y, dA[2 * q + 1].x, dA[2 * q + 1].y);
-    a.dD_part[r * Dm + c] = dD_acc;
-    a.db_part[r * Dm + c] = db_acc;
+    *reinterpret_cast<float4*>(dAp + q0) = make_float4(dA[0].x, dA[0].y, dA[1].x, dA[1].y);
+    *reinterpret_cast<float4*>(dAp + (q0 ^ 4)) = make_float4(dA[2].x, dA[2].y, dA[3].x, dA[3].y);
+    if (hs == 0) {
+      a.dD_part[r * Dm + c] = dD_acc;
+      a.db_part[r * Dm + c] = db_acc;
+    }
   }
 }
 
@@ -458,7 +495,7 @@ struct BwdAggLayout {
 };
 
 template <typename T, typename TBC, int G>
-__global__ void __launch_bounds__(kBThreads, 4) ssm_bwd_agg_kernel(const __grid_constant__ BwdLaunch P) {
+__global__ void __launch_bounds__(kAggThreads, 4) ssm_bwd_agg_kernel(const __grid_constant__ BwdLaunch P) {
   const BwdDir& a = P.dir[blockIdx.z / P.zdiv];
   const int seg = 1 + blockIdx.z % P.zdiv;  // segments 1 .. nseg-1
   extern __shared__ __align__(1024) unsigned char smem[];
@@ -539,7 +576,7 @@ __global__ void __launch_bounds__(kBThreads, 4) ssm_bwd_agg_kernel(const __grid_
       if (has_z) g *= act_f(ld_f(szo + row * kBTile), G);
       const float2 dy2 = dup2(valid ? g : 0.f), dt2 = dup2(dt);
       float2 Cq[8];
-      ld16q(sC + tl * kN, 0, Cq);
+      ld16(sC + tl * kN, Cq);
 #pragma unroll
       for (int p = 0; p < 8; ++p) {
         const float2 e = fmul2(A2[p], dt2);
