@@ -71,57 +71,102 @@ def read_traffic(name):
 
 
 class ClockSampler:
-    """nvidia-smi clock / throttle samples every 200 ms while running."""
+    """SM clock and throttle-reason samples taken in-process through NVML
+    (read-only queries) every 5 ms while the timed region runs, so even a
+    region of a few tens of milliseconds gets samples.  Falls back to an
+    nvidia-smi poller (200 ms) when NVML cannot be loaded."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    PERIOD_S = 0.005
+    NAMES = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
 
     def __init__(self, index):
         self.index = index
-        self.rows = []
+        self.rows = []  # (sm_mhz, max_mhz, set of active reason names)
+        self.stop = threading.Event()
+        self.thread = None
         self.proc = None
+        self.nvml = None
+
+    def _nvml_handle(self):
+        import pynvml
+        pynvml.nvmlInit()
+        try:  # the CUDA ordinal and NVML's index differ under CUDA_VISIBLE_DEVICES: match by PCI bus id
+            import torch
+            pr = torch.cuda.get_device_properties(self.index)
+            bus = f"{pr.pci_domain_id:08x}:{pr.pci_bus_id:02x}:{pr.pci_device_id:02x}.0"
+            h = pynvml.nvmlDeviceGetHandleByPciBusId(bus.encode())
+        except Exception:
+            h = pynvml.nvmlDeviceGetHandleByIndex(self.index)
+        bits = {"hw_slowdown": pynvml.nvmlClocksEventReasonHwSlowdown,
+                "hw_thermal_slowdown": pynvml.nvmlClocksEventReasonHwThermalSlowdown,
+                "sw_thermal_slowdown": pynvml.nvmlClocksEventReasonSwThermalSlowdown,
+                "sw_power_cap": pynvml.nvmlClocksEventReasonSwPowerCap}
+        mx = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
+        return pynvml, h, bits, mx
+
+    def _poll_nvml(self):
+        nv, h, bits, mx = self.nvml
+        while not self.stop.is_set():
+            try:
+                sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+                r = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                self.rows.append((float(sm), float(mx), {n for n, bit in bits.items() if r & bit}))
+            except Exception:
+                pass
+            self.stop.wait(self.PERIOD_S)
+
+    def _read_smi(self):
+        for line in self.proc.stdout:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 7 and parts[0].replace(".", "").isdigit():
+                self.rows.append((float(parts[0]), float(parts[1]),
+                                  {n for n, v in zip(self.NAMES, parts[3:7]) if v.lower() == "active"}))
 
     def __enter__(self):
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.nvml = self._nvml_handle()
+            self.thread = threading.Thread(target=self._poll_nvml, daemon=True)
+        except Exception:
+            self.nvml = None
+            fields = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+                      "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+                      "clocks_event_reasons.sw_power_cap")
+            try:
+                self.proc = subprocess.Popen(
+                    ["nvidia-smi", f"--id={self.index}", f"--query-gpu={fields}", "--format=csv,noheader,nounits",
+                     "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                self.thread = threading.Thread(target=self._read_smi, daemon=True)
+            except OSError:
+                self.thread = None
+        if self.thread:
             self.thread.start()
-        except OSError:
-            self.proc = None
         return self
 
     def wait_first(self, timeout=3.0):
         t0 = time.time()
-        while self.proc and not self.rows and time.time() - t0 < timeout:
-            time.sleep(0.02)
+        while self.thread and not self.rows and time.time() - t0 < timeout:
+            time.sleep(0.002)
         self.rows.clear()  # keep only samples taken during the timed region
 
-    def _read(self):
-        for line in self.proc.stdout:
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) >= 9:
-                self.rows.append(parts)
-
     def __exit__(self, *a):
+        self.stop.set()
         if self.proc:
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
             except subprocess.TimeoutExpired:
                 self.proc.kill()
+        if self.thread:
+            self.thread.join(timeout=5)
 
     def summary(self):
-        if not self.rows:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
-        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({n for r in self.rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(self.rows)}
+        rows = list(self.rows)
+        src = "nvml" if self.nvml else "nvidia-smi"
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0, "source": src}
+        return {"sm_mhz": statistics.median(r[0] for r in rows), "sm_max_mhz": max(r[1] for r in rows),
+                "reasons": sorted(set().union(*(r[2] for r in rows))), "samples": len(rows), "source": src,
+                "period_ms": self.PERIOD_S * 1e3 if self.nvml else 200}
 
 
 # ----------------------------------------------------------------------------- inputs

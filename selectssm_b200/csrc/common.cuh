@@ -17,7 +17,10 @@ void note_launches(unsigned n);
 constexpr int kChunk = 16;        // steps per TMA stage
 constexpr int kCk = 8;            // forward checkpoint spacing (backward register block)
 constexpr int kN = 16;            // state size supported by this build
-constexpr int kTileCh = 32;       // channels per forward CTA (the TMA box width)
+#ifndef SSM_FWD_TILE
+#define SSM_FWD_TILE 32
+#endif
+constexpr int kTileCh = SSM_FWD_TILE;  // channels per forward CTA (the TMA box width)
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 // Upper bound on polls of an mbarrier before a kernel gives up (each poll of

@@ -257,7 +257,10 @@ constexpr int kSMs = 148;
 // before it (quadratic in the segment count).  Its fitted sizes hold per
 // direction: a bidirectional launch (B=2, L=131072, 512 channels) ran faster with the
 // per-direction choice than with one that counts both directions' chains.
-constexpr SegPolicy kFwdSeg{64, false, kTileCh, 384, 1536, 0.55};
+#ifndef SSM_FWD_SLOTS
+#define SSM_FWD_SLOTS 384
+#endif
+constexpr SegPolicy kFwdSeg{64, false, kTileCh, SSM_FWD_SLOTS, 4 * SSM_FWD_SLOTS, 0.55};
 constexpr SegPolicy kBwdSeg{256, true, kBTile, 2L * kSMs, 4L * kSMs, 0.5};
 
 static Seg choose_segments(const Geo& g, SegPolicy pol) {
@@ -410,7 +413,7 @@ static int launch_fwd_t(FwdLaunch& L, int ndir, const Geo& g, cudaStream_t s) {
   }
   L.zdiv = nseg;
   grid.z = ndir * nseg;
-  const bool wide = (long)grid.x * grid.y * grid.z <= 3L * kSMs;
+  const bool wide = (long)grid.x * grid.y * grid.z <= (long)(kFMinBlocks / 2) * kSMs;
   auto kern = wide ? ssm_fwd_kernel<T, TBC, false, true> : ssm_fwd_kernel<T, TBC, false, false>;
   SSM_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kBytes),
                  "cudaFuncSetAttribute(ssm_fwd_kernel)");

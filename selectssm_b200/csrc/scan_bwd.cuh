@@ -138,6 +138,38 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const float (&v)[16]) 
       : "memory");
 }
 
+// TMEM store / load without a memory clobber, so the compiler may move
+// shared-memory loads and shuffles across them; a load's registers are tied
+// to the wait that completes it (tmem_wait_ld_regs), so no use of them can be
+// scheduled before that wait.
+__device__ __forceinline__ void tmem_st16_nc(uint32_t taddr, const float (&v)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+          taddr),
+      "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
+      "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
+      "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])),
+      "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+      "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
+      "r"(__float_as_uint(v[15])));
+}
+__device__ __forceinline__ void tmem_ld16_nc(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void sts_nc(float* p, float v) {
+  asm volatile("st.shared.f32 [%0], %1;" ::"r"(smem_u32(p)), "f"(v));
+}
+__device__ __forceinline__ void tmem_wait_ld_regs(uint32_t (&r)[16]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                 "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                 "+r"(r[15]));
+}
+
 // G: the gate activation (an ssm_act code), fixed per launch so the step loops
 // hold no branch on it.
 // MC: dB / dC partial sums go to NVLink multicast addresses (cross-GPU sum);
@@ -343,9 +375,9 @@ __global__ void __launch_bounds__(kBThreads, 2) ssm_bwd_kernel(const __grid_cons
           keep[8 + 2 * p] = q.x;
           keep[8 + 2 * p + 1] = q.y;
         }
-        tmem_st16(trow + u * 16, keep);
+        tmem_st16_nc(trow + u * 16, keep);
         const float dc = reduce16ch(vc, b2, b1);
-        if (red_writer) red[(warp * kChunk + tl) * 32 + kN + red_n] = dc;
+        if (red_writer) sts_nc(red + (warp * kChunk + tl) * 32 + kN + red_n, dc);
         float y = y2.x + y2.y;
         y += __shfl_xor_sync(kFull, y, 16);
         if (u & 1) yo[u >> 1] = own_odd ? y : yo[u >> 1];
@@ -356,12 +388,12 @@ __global__ void __launch_bounds__(kBThreads, 2) ssm_bwd_kernel(const __grid_cons
       // ---- adjoint sweep (TMEM reads double buffered one step ahead)
       float sbfo[kCk / 2], sawo[kCk / 2];
       uint32_t buf[2][16];
-      tmem_ld16(trow + (kCk - 1) * 16, buf[(kCk - 1) & 1]);
-      tmem_wait_ld();
+      tmem_ld16_nc(trow + (kCk - 1) * 16, buf[(kCk - 1) & 1]);
+      tmem_wait_ld_regs(buf[(kCk - 1) & 1]);
 #pragma unroll
       for (int u = kCk - 1; u >= 0; --u) {
         const int tl = T0 + u;
-        if (u > 0) tmem_ld16(trow + (u - 1) * 16, buf[(u - 1) & 1]);
+        if (u > 0) tmem_ld16_nc(trow + (u - 1) * 16, buf[(u - 1) & 1]);
         float2 Bq[4], Cq[4];
         ld8q(sB + tl * kN, q0, Bq);
         ld8q(sC + tl * kN, q0, Cq);
@@ -381,7 +413,7 @@ __global__ void __launch_bounds__(kBThreads, 2) ssm_bwd_kernel(const __grid_cons
           fa[p] = fmul2(f, al);
         }
         const float db = reduce16ch(vb, b2, b1);
-        if (red_writer) red[(warp * kChunk + tl) * 32 + red_n] = db;
+        if (red_writer) sts_nc(red + (warp * kChunk + tl) * 32 + red_n, db);
         float sbf = sBf.x + sBf.y, saw = sAw.x + sAw.y;
         sbf += __shfl_xor_sync(kFull, sbf, 16);
         saw += __shfl_xor_sync(kFull, saw, 16);
@@ -392,8 +424,9 @@ __global__ void __launch_bounds__(kBThreads, 2) ssm_bwd_kernel(const __grid_cons
           sbfo[u >> 1] = own_odd ? sbfo[u >> 1] : sbf;
           sawo[u >> 1] = own_odd ? sawo[u >> 1] : saw;
         }
-        if (u > 0) tmem_wait_ld();
+        if (u > 0) tmem_wait_ld_regs(buf[(u - 1) & 1]);
       }
+
       // ---- epilogue of this lane's own steps: du, ddelta, dz and the skip
       // gradients (straight-line; steps past L and lanes past Dm hold zeros,
       // only the stores are predicated)

@@ -36,7 +36,8 @@ namespace ssm {
 
 
 
-constexpr int kFThreads = 128;  // 4 warps x 8 channels = kTileCh
+constexpr int kFThreads = 4 * kTileCh;  // 4 lanes per channel, 8 channels per warp
+constexpr int kFMinBlocks = 768 / kFThreads;  // resident CTAs per SM at <= 80 registers
 constexpr int kFStages = 3;
 
 template <typename T, typename TBC>
@@ -54,7 +55,7 @@ struct FwdSmem {
 // WIDE: the grid fills at most 3 CTAs per SM, so each thread may use up to 168
 // registers (more scheduling freedom); otherwise 6 CTAs per SM fit (80).
 template <typename T, typename TBC, bool AGG, bool WIDE = false>
-__global__ void __launch_bounds__(kFThreads, WIDE ? 3 : 6) ssm_fwd_kernel(const __grid_constant__ FwdLaunch P) {
+__global__ void __launch_bounds__(kFThreads, WIDE ? kFMinBlocks / 2 : kFMinBlocks) ssm_fwd_kernel(const __grid_constant__ FwdLaunch P) {
   using S = FwdSmem<T, TBC>;
   const FwdDir& a = P.dir[blockIdx.z / P.zdiv];
   const int seg = blockIdx.z % P.zdiv;
