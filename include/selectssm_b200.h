@@ -231,6 +231,16 @@ SSM_API int ssm_rmsnorm_bwd(const ssm_norm_params_t* p, ssm_stream_t stream);
  * returns, leaving the context usable.  No counterpart in the reference. */
 SSM_API int ssm_selftest_wait_timeout(int32_t* status, uint32_t spin_limit, ssm_stream_t stream);
 
+/* Failure-path self-test of the backward's decoupled lookback: runs ssm_bwd
+ * on p (which must describe a shape the backward cuts into segments, with
+ * p->status set; otherwise SSM_ERR_SHAPE / SSM_ERR_NULL) but leaves out the
+ * CTAs of the last segment, so the segment before it waits for a flag that is
+ * never set.  Every wait gives up after spin_limit polls (1 .. 2^22), the
+ * kernel writes SSM_ERR_TIMEOUT to *p->status and returns, and the context
+ * stays usable.  The gradients it writes are undefined.  No counterpart in the
+ * reference. */
+SSM_API int ssm_selftest_lookback_timeout(const ssm_params_t* p, uint32_t spin_limit, ssm_stream_t stream);
+
 /* Message for a status code (static storage). */
 SSM_API const char* ssm_strerror(int status);
 /* ---- backward without any device allocation ----

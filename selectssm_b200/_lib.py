@@ -44,6 +44,7 @@ EXPORTED_SYMBOLS = (
     "ssm_version", "ssm_bwd_noalloc", "ssm_launch_count",
     "ssm_rmsnorm_workspace_bytes", "ssm_rmsnorm_fwd", "ssm_rmsnorm_bwd", "ssm_selftest_wait_timeout",
     "ssm_bwd_bc_multicast", "ssm_bwd_workspace_bytes", "ssm_fwd_workspace_bytes",
+    "ssm_selftest_lookback_timeout",
 )
 
 
@@ -131,6 +132,7 @@ def load(path: str | None = None) -> ctypes.CDLL:
         "ssm_rmsnorm_fwd": (ctypes.c_int, [NP, ctypes.c_void_p]),
         "ssm_rmsnorm_bwd": (ctypes.c_int, [NP, ctypes.c_void_p]),
         "ssm_selftest_wait_timeout": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_uint32, ctypes.c_void_p]),
+        "ssm_selftest_lookback_timeout": (ctypes.c_int, [ctypes.POINTER(SSMParams), ctypes.c_uint32, ctypes.c_void_p]),
         "ssm_strerror": (ctypes.c_char_p, [ctypes.c_int]),
         "ssm_last_error": (ctypes.c_char_p, []),
         "ssm_version": (ctypes.c_char_p, []),

@@ -1,6 +1,7 @@
 // C-ABI entry points for the selective scan (forward, backward, bidirectional),
 // their argument checks, TMA descriptor set-up and launch sequences.
 #include <algorithm>
+#include <cstdlib>
 #include <cstdio>
 #include <cstring>
 #include <atomic>
@@ -248,6 +249,8 @@ struct SegPolicy {
   long slots;       // resident CTAs of the main kernel on the GPU
   long agg_slots;   // resident CTAs of the pre-pass
   double agg_cost;  // pre-pass cost of one stage relative to the main kernel's
+  bool single_pass; // pre-pass inside the main launch (decoupled lookback)
+  double cta_cost;  // fixed cost of one CTA in stages (set-up, pipeline fill, lookback)
 };
 constexpr int kSMs = 148;
 // The forward's CTAs are small and latency bound, so its "waves" are effective
@@ -260,12 +263,25 @@ constexpr int kSMs = 148;
 #ifndef SSM_FWD_SLOTS
 #define SSM_FWD_SLOTS 384
 #endif
-constexpr SegPolicy kFwdSeg{64, false, kTileCh, SSM_FWD_SLOTS, 4 * SSM_FWD_SLOTS, 0.55};
-constexpr SegPolicy kBwdSeg{256, true, kBTile, 2L * kSMs, 4L * kSMs, 0.5};
+constexpr SegPolicy kFwdSeg{64, false, kTileCh, SSM_FWD_SLOTS, 4 * SSM_FWD_SLOTS, 0.55, false, 0.0};
+// The backward runs its aggregate passes inside the main launch, so CTAs of
+// all segments share the GPU: the model is the total work spread over the
+// resident CTAs plus the duration of the last CTA (the tail), with a fixed
+// cost per CTA.
+constexpr SegPolicy kBwdSeg{256, true, kBTile, 2L * kSMs, 2L * kSMs, 0.35, true, 8.0};
 
 static Seg choose_segments(const Geo& g, SegPolicy pol) {
   const int nblk = (g.L + kChunk - 1) / kChunk;
   if (nblk == 0) return {1, 1};
+#ifdef SSM_EXP_ENV
+  if (const char* e = getenv(pol.tile == kBTile ? "SSM_BWD_NSEG" : "SSM_FWD_NSEG")) {
+    int n = atoi(e);
+    if (n < 1) n = 1;
+    if (n > nblk) n = nblk;
+    const int sc = (nblk + n - 1) / n;
+    return {(nblk + sc - 1) / sc, sc};
+  }
+#endif
   // both directions of a bidirectional call share the launch
   const long chains = (long)((g.Dm + pol.tile - 1) / pol.tile) * g.B * (pol.per_launch ? g.ndir : 1);
   if (chains <= 0) return {1, nblk};
@@ -278,9 +294,16 @@ static Seg choose_segments(const Geo& g, SegPolicy pol) {
     const int seg_chunks = (nblk + n - 1) / n;
     const int nseg = (nblk + seg_chunks - 1) / seg_chunks;
     if (nseg != n) continue;  // the same split as a smaller n
-    const long waves = (chains * nseg + pol.slots - 1) / pol.slots;
-    const long agg_waves = (chains * (nseg - 1) + pol.agg_slots - 1) / pol.agg_slots;
-    const double cost = (double)waves * seg_chunks + pol.agg_cost * (double)agg_waves * seg_chunks + 0.25 * nseg;
+    double cost;
+    if (pol.single_pass) {
+      const double per_cta = seg_chunks * (1.0 + (nseg > 1 ? pol.agg_cost : 0.0)) + pol.cta_cost;
+      const double work = (double)chains * (seg_chunks * (nseg + pol.agg_cost * (nseg - 1)) + pol.cta_cost * nseg);
+      cost = work / pol.slots + per_cta;
+    } else {
+      const long waves = (chains * nseg + pol.slots - 1) / pol.slots;
+      const long agg_waves = (chains * (nseg - 1) + pol.agg_slots - 1) / pol.agg_slots;
+      cost = (double)waves * seg_chunks + pol.agg_cost * (double)agg_waves * seg_chunks + 0.25 * nseg;
+    }
     if (n == 1 || cost < best) {
       best = cost;
       pick = {nseg, seg_chunks};
@@ -308,11 +331,18 @@ static size_t bc_part_bytes(const Geo& g) {
   return round256((size_t)((g.Dm + kBTile - 1) / kBTile) * g.B * g.L * 2 * kN * 4);
 }
 
+// lookback flags of one direction: a 16-byte word (the launch's CTA ticket,
+// used in the first direction's region) then one int per (row, tile, segment)
+static size_t bwd_flag_bytes(const Geo& g, int nseg) {
+  return round256(16 + (size_t)g.B * ((g.Dm + kBTile - 1) / kBTile) * nseg * 4);
+}
+
 static size_t bwd_ws_bytes(const Geo& g, bool multicast = false) {
   const Seg sg = choose_segments(g, kBwdSeg);
   const size_t rows = (size_t)g.B * sg.nseg * g.Dm;
   size_t n = round256(rows * kN * 4) + 2 * round256(rows * 4);
-  if (sg.nseg > 1) n += round256(rows * kN * 4) + round256(rows * 4);  // segF, segT
+  if (sg.nseg > 1)  // segF, segT, segI, flags
+    n += 2 * round256(rows * kN * 4) + round256(rows * 4) + bwd_flag_bytes(g, sg.nseg);
   if (!multicast) n += bc_part_bytes(g);  // the multicast form sums dB / dC in the caller's buffer
   return n + wide_bc_bytes(g);
 }
@@ -431,7 +461,9 @@ static int launch_fwd(FwdLaunch& L, int ndir, const Geo& g, cudaStream_t s) {
 
 // ---------------------------------------------------------------- backward launch
 struct BwdWs {
-  float *dA_part, *dD_part, *db_part, *bc_part, *dB_acc, *dC_acc, *segF, *segT, *Bw, *Cw;
+  float *dA_part, *dD_part, *db_part, *bc_part, *dB_acc, *dC_acc, *segF, *segT, *segI, *Bw, *Cw;
+  int* flags;  // ticket word, then the lookback flags (null without segments)
+  size_t flag_bytes;
   int64_t acc_stride;
 };
 
@@ -444,12 +476,19 @@ static void carve_ws(const ssm_params_t* p, const Geo& g, char* ws, BwdWs* w, fl
   ws += round256(rows * 4);
   w->db_part = reinterpret_cast<float*>(ws);
   ws += round256(rows * 4);
-  w->segF = w->segT = nullptr;
+  w->segF = w->segT = w->segI = nullptr;
+  w->flags = nullptr;
+  w->flag_bytes = 0;
   if (sg.nseg > 1) {
     w->segF = reinterpret_cast<float*>(ws);
     ws += round256(rows * kN * 4);
     w->segT = reinterpret_cast<float*>(ws);
     ws += round256(rows * 4);
+    w->segI = reinterpret_cast<float*>(ws);
+    ws += round256(rows * kN * 4);
+    w->flags = reinterpret_cast<int*>(ws);
+    w->flag_bytes = bwd_flag_bytes(g, sg.nseg);
+    ws += w->flag_bytes;
   }
   w->bc_part = w->dB_acc = w->dC_acc = nullptr;
   w->acc_stride = kN;
@@ -514,11 +553,21 @@ static int fill_bwd_dir(const ssm_params_t* p, const Geo& g, const BwdWs& w, Bwd
   d->seg_chunks = sg.seg_chunks;
   d->segF = w.segF;
   d->segT = w.segT;
+  d->segI = w.segI;
+  d->seg_flag = w.flags ? w.flags + 4 : nullptr;
   return SSM_OK;
 }
 
+// Test hook of the lookback failure path: the launch leaves out the CTAs of
+// the last segment (their tickets are skipped), so the segment before it
+// waits for a flag that is never set and gives up after spin_limit polls.
+struct BwdHook {
+  uint32_t spin_limit;
+  bool drop_last_segment;
+};
+
 template <typename T, typename TBC, int G>
-static int launch_bwd_t(BwdLaunch& L, int ndir, const Geo& g, cudaStream_t s) {
+static int launch_bwd_t(BwdLaunch& L, int ndir, const Geo& g, cudaStream_t s, const BwdHook* hook) {
   int bytes = 0;
   for (int d = 0; d < ndir; ++d) {
     const BwdDir& a = L.dir[d];
@@ -528,30 +577,21 @@ static int launch_bwd_t(BwdLaunch& L, int ndir, const Geo& g, cudaStream_t s) {
   }
   const int nseg = L.dir[0].nseg;
   dim3 grid((g.Dm + kBTile - 1) / kBTile, g.B, 1);
-  if (nseg > 1) {  // segment pre-pass: adjoint carried out of every segment but the first
-    int abytes = 0;
-    for (int d = 0; d < ndir; ++d) {
-      const BwdAggLayout al(sizeof(T), sizeof(TBC), L.dir[d].has_z != 0);
-      abytes = al.bytes > abytes ? al.bytes : abytes;
-    }
-    auto agg = ssm_bwd_agg_kernel<T, TBC, G>;
-    SSM_CUDA_CHECK(cudaFuncSetAttribute(agg, cudaFuncAttributeMaxDynamicSharedMemorySize, abytes),
-                   "cudaFuncSetAttribute(ssm_bwd_agg_kernel)");
-    L.zdiv = nseg - 1;
-    grid.z = ndir * (nseg - 1);
-    agg<<<grid, kAggThreads, abytes, s>>>(L);
-    note_launches(1);
-  SSM_CUDA_CHECK(cudaGetLastError(), "launch ssm_bwd_agg_kernel");
-    dim3 fgrid((g.Dm * kN + 255) / 256, ndir, g.B);
-    ssm_bwd_fold_kernel<<<fgrid, 256, 0, s>>>(L);
-    note_launches(1);
-  SSM_CUDA_CHECK(cudaGetLastError(), "launch ssm_bwd_fold_kernel");
-  }
   auto kern = L.dir[0].bc_mode == kBcMulticast ? ssm_bwd_kernel<T, TBC, G, true> : ssm_bwd_kernel<T, TBC, G, false>;
   SSM_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes),
                  "cudaFuncSetAttribute(ssm_bwd_kernel)");
   L.zdiv = nseg;
   grid.z = ndir * nseg;
+  L.ntile = (int)grid.x;
+  L.batch = g.B;
+  L.chains = (int)grid.x * g.B * ndir;
+  if (hook) {
+    L.spin_limit = hook->spin_limit;
+    if (hook->drop_last_segment) {
+      grid.z = ndir * (nseg - 1);
+      L.ticket_base = L.chains;
+    }
+  }
   kern<<<grid, kBThreads, bytes, s>>>(L);
   note_launches(1);
   SSM_CUDA_CHECK(cudaGetLastError(), "launch ssm_bwd_kernel");
@@ -559,24 +599,27 @@ static int launch_bwd_t(BwdLaunch& L, int ndir, const Geo& g, cudaStream_t s) {
 }
 
 template <typename T, typename TBC>
-static int launch_bwd_g(BwdLaunch& L, int ndir, const Geo& g, cudaStream_t s) {
+static int launch_bwd_g(BwdLaunch& L, int ndir, const Geo& g, cudaStream_t s, const BwdHook* hook) {
   switch (L.dir[0].gate_act) {
-    case SSM_ACT_SILU: return launch_bwd_t<T, TBC, SSM_ACT_SILU>(L, ndir, g, s);
-    case SSM_ACT_GELU: return launch_bwd_t<T, TBC, SSM_ACT_GELU>(L, ndir, g, s);
-    case SSM_ACT_RELU: return launch_bwd_t<T, TBC, SSM_ACT_RELU>(L, ndir, g, s);
-    default: return launch_bwd_t<T, TBC, SSM_ACT_NONE>(L, ndir, g, s);
+    case SSM_ACT_SILU: return launch_bwd_t<T, TBC, SSM_ACT_SILU>(L, ndir, g, s, hook);
+    case SSM_ACT_GELU: return launch_bwd_t<T, TBC, SSM_ACT_GELU>(L, ndir, g, s, hook);
+    case SSM_ACT_RELU: return launch_bwd_t<T, TBC, SSM_ACT_RELU>(L, ndir, g, s, hook);
+    default: return launch_bwd_t<T, TBC, SSM_ACT_NONE>(L, ndir, g, s, hook);
   }
 }
 
-static int launch_bwd(BwdLaunch& L, int ndir, const Geo& g, cudaStream_t s) {
+static int launch_bwd(BwdLaunch& L, int ndir, const Geo& g, cudaStream_t s, const BwdHook* hook) {
   if (ndir == 2 && L.dir[0].gate_act != L.dir[1].gate_act) {  // one launch per gate
     BwdLaunch L1 = L;
     L1.dir[0] = L.dir[1];
-    const int st = launch_bwd(L, 1, g, s);
-    return st ? st : launch_bwd(L1, 1, g, s);
+    if (L.ticket) {  // the second launch takes its tickets from the second direction's word
+      L1.ticket = L.dir[1].seg_flag - 4;
+    }
+    const int st = launch_bwd(L, 1, g, s, hook);
+    return st ? st : launch_bwd(L1, 1, g, s, hook);
   }
-  if (g.bf16) return launch_bwd_g<__nv_bfloat16, float>(L, ndir, g, s);  // B / C widened to float32
-  return launch_bwd_g<float, float>(L, ndir, g, s);
+  if (g.bf16) return launch_bwd_g<__nv_bfloat16, float>(L, ndir, g, s, hook);  // B / C widened to float32
+  return launch_bwd_g<float, float>(L, ndir, g, s, hook);
 }
 
 static int launch_finalize(const ssm_params_t* p, const Geo& g, const BwdWs& w, cudaStream_t s, bool reduced) {
@@ -680,7 +723,8 @@ int ssm_fwd_bidir(const ssm_params_t* fwd, const ssm_params_t* rev, ssm_stream_t
 }
 
 namespace ssm {
-static int bwd_impl(const ssm_params_t* fwd, const ssm_params_t* rev, float* dbc_mc, ssm_stream_t stream) {
+static int bwd_impl(const ssm_params_t* fwd, const ssm_params_t* rev, float* dbc_mc, ssm_stream_t stream,
+                    const BwdHook* hook = nullptr) {
   Geo g, g2;
   int st = check_bwd(fwd, &g);
   if (st) return st;
@@ -717,8 +761,13 @@ static int bwd_impl(const ssm_params_t* fwd, const ssm_params_t* rev, float* dbc
   for (int d = 0; d < ndir; ++d) {
     st = fill_bwd_dir(ps[d], g, w[d], &args.dir[d], s, dbc_mc != nullptr);
     if (st) return st;
+    if (w[d].flags)  // lookback flags (and the ticket) start at zero on every call
+      SSM_CUDA_CHECK(cudaMemsetAsync(w[d].flags, 0, w[d].flag_bytes, s), "cudaMemsetAsync(lookback flags)");
   }
-  st = launch_bwd(args, ndir, g, s);
+  args.ticket = w[0].flags;
+  args.spin_limit = kLookbackSpin;
+  if (hook && (!w[0].flags || hook->spin_limit == 0)) return SSM_ERR_SHAPE;  // the self-test needs segments
+  st = launch_bwd(args, ndir, g, s, hook);
   if (st) return st;
   for (int d = 0; d < ndir; ++d) {
     st = launch_finalize(ps[d], g, w[d], s, dbc_mc != nullptr);
@@ -743,6 +792,13 @@ int ssm_bwd_bc_multicast(const ssm_params_t* p, float* dbc_mc, ssm_stream_t stre
   q.dB = dbc_mc;
   q.dC = dbc_mc;
   return bwd_impl(&q, nullptr, dbc_mc, stream);
+}
+
+int ssm_selftest_lookback_timeout(const ssm_params_t* p, uint32_t spin_limit, ssm_stream_t stream) {
+  if (!p || !p->status) return SSM_ERR_NULL;
+  if (spin_limit == 0 || spin_limit > kLookbackSpin) return SSM_ERR_SHAPE;
+  const BwdHook hook{spin_limit, true};
+  return bwd_impl(p, nullptr, nullptr, stream, &hook);
 }
 
 const char* ssm_strerror(int status) {

@@ -35,11 +35,15 @@
 //   The gate activation is a template parameter (fixed per launch) and the
 //   per-step work holds no data- or flag-dependent branch (only stores are
 //   predicated), so the compiler can schedule across the unrolled steps.
-// Segments: ssm_bwd_agg_kernel runs segments 1..S-1 from a zero adjoint and
-//   writes the adjoint carried out of each one's first step (one lane per
-//   channel, 16 states; one state pair per lane evaluates its exponential on
-//   the FMA pipe to relieve the MUFU unit); ssm_bwd_fold_kernel turns those
-//   into the carry entering each segment.
+// Segments: with few (batch row, channel tile) chains the sequence is cut into
+//   segments run by separate CTAs in one launch (single-pass decoupled
+//   lookback).  A CTA takes its segment from an atomic ticket, last segment
+//   first; for a segment that an earlier one waits on it first runs the
+//   adjoint over its own steps from a zero carry (the aggregate pass: delta, C,
+//   dout, z only) and publishes that carry and its sum of dt under a flag; it
+//   then folds the published values of the later segments (bounded waits) into
+//   the carry entering its own last step, publishes its inclusive carry, and
+//   runs the main pass from it.
 #pragma once
 
 #include "scan_kernels.cuh"
@@ -51,7 +55,6 @@ constexpr int kBWarps = kBTile / 16;                   // 16 channels per warp
 constexpr int kBThreads = 2 * kBTile;
 constexpr int kBStages = 2;
 constexpr uint32_t kBTmemCols = 2 * kCk * kN;          // 2 warp groups x 8 steps x (8 alpha + 8 alpha*h)
-constexpr int kAggThreads = kBTile;                    // pre-pass: one lane per channel
 
 // Shared-memory layout (bytes), sized at run time: the output-frame copy of u
 // and the scan-frame copies of dout / z only exist for the reverse direction
@@ -77,6 +80,9 @@ struct BwdLayout {
     offTmem = offBars + 8 * kBStages;
     bytes = offTmem + 16;
   }
+  // The CTA's ticket is broadcast through the first word of shared memory
+  // (stage 0's u tile): it is read before the first TMA load is issued.
+  static constexpr int kTicketSlot = 0;
   __host__ __device__ static uint32_t tx(int es, int esbc, bool has_z, bool mirror) {
     const int act = kChunk * kBTile * es, bc = kChunk * kN * esbc;
     return 3 * act + 2 * bc + (has_z ? act : 0) + (mirror ? (has_z ? 3 : 2) * act : 0);
@@ -112,17 +118,6 @@ __device__ __forceinline__ void ld8q(const TB* row, int q0, float2 (&v)[4]) {
   v[1] = make_float2(f0.z, f0.w);
   v[2] = make_float2(f1.x, f1.y);
   v[3] = make_float2(f1.z, f1.w);
-}
-
-// 16 per-state values in natural order -> 8 pairs
-template <typename TB>
-__device__ __forceinline__ void ld16(const TB* row, float2 (&v)[8]) {
-#pragma unroll
-  for (int q = 0; q < 4; ++q) {
-    const float4 f = ld4(row + 4 * q);
-    v[2 * q] = make_float2(f.x, f.y);
-    v[2 * q + 1] = make_float2(f.z, f.w);
-  }
 }
 
 __device__ __forceinline__ void tmem_st16(uint32_t taddr, const float (&v)[16]) {
@@ -176,12 +171,25 @@ __device__ __forceinline__ void tmem_wait_ld_regs(uint32_t (&r)[16]) {
 // a template parameter so the single-GPU instance carries no trace of it.
 template <typename T, typename TBC, int G, bool MC = false>
 __global__ void __launch_bounds__(kBThreads, 2) ssm_bwd_kernel(const __grid_constant__ BwdLaunch P) {
-  const BwdDir& a = P.dir[blockIdx.z / P.zdiv];
-  const int seg = blockIdx.z % P.zdiv;
   extern __shared__ __align__(1024) unsigned char smem[];
+  // CTA identity: with segments, from an atomic ticket in scan order (the last
+  // segments first, so every segment a CTA waits for is already running);
+  // otherwise from the block index.  Grid: (channel tiles, batch, directions x segments).
+  int tile = blockIdx.x, b = blockIdx.y, dz = blockIdx.z;
+  if (P.ticket) {
+    int* slot = reinterpret_cast<int*>(smem + BwdLayout::kTicketSlot);
+    if (threadIdx.x == 0) *slot = atomicAdd(P.ticket, 1) + P.ticket_base;
+    __syncthreads();
+    const int k = *slot;
+    const int r = k % P.chains;
+    tile = r % P.ntile;
+    b = (r / P.ntile) % P.batch;
+    dz = (r / (P.ntile * P.batch)) * P.zdiv + (P.zdiv - 1 - k / P.chains);
+  }
+  const BwdDir& a = P.dir[dz / P.zdiv];
+  const int seg = dz % P.zdiv;
 
-  const int b = blockIdx.y;
-  const int c0 = blockIdx.x * kBTile;
+  const int c0 = tile * kBTile;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int hs = lane >> 4;                   // state half of this lane
   const int cl = warp * 16 + (lane & 15);     // channel within the tile
@@ -219,20 +227,30 @@ __global__ void __launch_bounds__(kBThreads, 2) ssm_bwd_kernel(const __grid_cons
   // this warp's lane quarter and column half
   const uint32_t trow = tbase + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)((warp >> 2) * kCk * kN);
 
+  // Loads: first the aggregate pass over the segment (segments that a later
+  // CTA waits for; delta, C, dout, z only), then the main pass, each visiting
+  // the chunks last to first; load g uses stage g % 2.
+  const bool lookback = a.nseg > 1;
+  const int nagg = (lookback && seg > 0) ? nloc : 0;
+  const int ntot = nagg + nloc;
   const uint32_t tx = BwdLayout::tx(sizeof(T), sizeof(TBC), has_z, mirror);
-  auto issue = [&](int it) {  // it-th load is chunk j1-1-it (last first)
-    const int j = j1 - 1 - it;
-    unsigned char* st = smem + (it % kBStages) * S.stage;
-    uint64_t* bar = &bars[it % kBStages];
+  const uint32_t tx_agg = 2 * kChunk * kBTile * (int)sizeof(T) + kChunk * kN * (int)sizeof(TBC) +
+                          (has_z ? kChunk * kBTile * (int)sizeof(T) : 0);
+  auto issue = [&](int g) {
+    const bool ag = g < nagg;
+    const int j = j1 - 1 - (ag ? g : g - nagg);
+    unsigned char* st = smem + (g % kBStages) * S.stage;
+    uint64_t* bar = &bars[g % kBStages];
     const int t0 = j * kChunk;
     const int ot0 = rev ? L - kChunk - t0 : t0;
-    mbar_arrive_expect_tx(bar, tx);
-    tma_load_3d(st + S.offU, &a.tm_u, bar, c0, t0, b);
+    mbar_arrive_expect_tx(bar, ag ? tx_agg : tx);
     tma_load_3d(st + S.offDelta, &a.tm_delta, bar, c0, t0, b);
-    tma_load_3d(st + S.offB, &a.tm_B, bar, 0, t0, b);
     tma_load_3d(st + S.offC, &a.tm_C, bar, 0, t0, b);
     tma_load_3d(st + S.offDo, &a.tm_dout, bar, oc0, ot0, b);
     if (has_z) tma_load_3d(st + S.offZo, &a.tm_z, bar, oc0, ot0, b);
+    if (ag) return;
+    tma_load_3d(st + S.offU, &a.tm_u, bar, c0, t0, b);
+    tma_load_3d(st + S.offB, &a.tm_B, bar, 0, t0, b);
     if (mirror) {
       tma_load_3d(st + S.offUo, &a.tm_u, bar, oc0, ot0, b);
       tma_load_3d(st + S.offDs, &a.tm_dout, bar, c0, t0, b);
@@ -240,8 +258,8 @@ __global__ void __launch_bounds__(kBThreads, 2) ssm_bwd_kernel(const __grid_cons
     }
   };
   if (threadIdx.x == 0) {
-    const int npre = nloc < kBStages ? nloc : kBStages;
-    for (int it = 0; it < npre; ++it) issue(it);
+    const int npre = ntot < kBStages ? ntot : kBStages;
+    for (int g = 0; g < npre; ++g) issue(g);
   }
 
   // state layout (see reduce16ch / ld8q)
@@ -264,8 +282,6 @@ __global__ void __launch_bounds__(kBThreads, 2) ssm_bwd_kernel(const __grid_cons
   float2 fa[4], dA[4];  // f_{t+1} alpha_{t+1} carried backwards; dA accumulators (A log2 e frame)
 #pragma unroll
   for (int p = 0; p < 4; ++p) fa[p] = dA[p] = make_float2(0.f, 0.f);
-  if (a.nseg > 1 && cvalid)  // adjoint entering this segment from the later ones
-    ld8q(a.segF + (((size_t)b * a.nseg + seg) * Dm + c) * kN, q0, fa);
   float dD_acc = 0.f, db_acc = 0.f;
   T* du_g = reinterpret_cast<T*>(a.du) + (size_t)b * L * Dm + c;
   T* dd_g = reinterpret_cast<T*>(a.ddelta) + (size_t)b * L * Dm + c;
@@ -273,10 +289,147 @@ __global__ void __launch_bounds__(kBThreads, 2) ssm_bwd_kernel(const __grid_cons
   const float* st_b = a.states + ((size_t)b * nck * Dm + (cvalid ? c : 0)) * kN;
   bool failed = false;
 
-  for (int it = 0; it < nloc; ++it) {
+  // ---- aggregate pass: the adjoint over this segment from a zero carry; the
+  // carry it leaves at the segment's first step and the segment's sum of dt
+  // are what the segment before it folds in (src/selectssm/ssmrecscan.py:121-133
+  // chains chunk adjoints the same way).
+  float tsum = 0.f;
+  for (int g = 0; g < nagg; ++g) {
+    const int j = j1 - 1 - g;
+    const int s = g % kBStages;
+    const bool ok = mbar_wait_bounded(&bars[s], (g / kBStages) & 1);
+    if (!__syncthreads_and(ok)) {
+      failed = true;
+      break;
+    }
+    const unsigned char* st = smem + s * S.stage;
+    const T* sd = reinterpret_cast<const T*>(st + S.offDelta) + cl;
+    const T* szo = reinterpret_cast<const T*>(st + S.offZo) + col;
+    const T* sdo = reinterpret_cast<const T*>(st + S.offDo) + col;
+    const TBC* sC = reinterpret_cast<const TBC*>(st + S.offC);
+#pragma unroll 1
+    for (int blk = 1; blk >= 0; --blk) {
+      const int T0 = blk * kCk;
+      float dtv[kCk], dyv[kCk];
+#pragma unroll
+      for (int k = 0; k < kCk / 2; ++k) {
+        const int tl = T0 + 2 * k + hs;
+        const bool valid = j * kChunk + tl < L;
+        const float dr = ld_f(sd + tl * kBTile) + bias;
+        float dt = softplus ? softplus_f(dr) : dr;
+        dt = valid ? dt : 0.f;
+        tsum += dt;
+        const int row = rev ? kChunk - 1 - tl : tl;
+        float gv = ld_f(sdo + row * kBTile);
+        if (has_z) gv *= act_f(ld_f(szo + row * kBTile), G);
+        const float dy = valid ? gv : 0.f;
+        const float pdt = __shfl_xor_sync(kFull, dt, 16);
+        const float pdy = __shfl_xor_sync(kFull, dy, 16);
+        dtv[2 * k] = own_odd ? pdt : dt;
+        dtv[2 * k + 1] = own_odd ? dt : pdt;
+        dyv[2 * k] = own_odd ? pdy : dy;
+        dyv[2 * k + 1] = own_odd ? dy : pdy;
+      }
+#pragma unroll
+      for (int u = kCk - 1; u >= 0; --u) {
+        float2 Cq[4];
+        ld8q(sC + (T0 + u) * kN, q0, Cq);
+        const float2 dt2 = dup2(dtv[u]), dy2 = dup2(dyv[u]);
+#pragma unroll
+        for (int p = 0; p < 4; ++p) {
+          const float2 e = fmul2(A2[p], dt2);
+          fa[p] = fmul2(ffma2(Cq[p], dy2, fa[p]), make_float2(ex2(e.x), ex2(e.y)));
+        }
+      }
+    }
+    __syncthreads();  // stage s consumed
+    if (threadIdx.x == 0 && g + kBStages < ntot) {
+      fence_proxy_async_smem();
+      issue(g + kBStages);
+    }
+  }
+  int* wait_slot = reinterpret_cast<int*>(smem + S.offTmem + 8);
+  const size_t seg_row = (size_t)b * a.nseg + seg;
+  int* my_flag = a.seg_flag + ((size_t)b * P.ntile + tile) * a.nseg + seg;
+  if (lookback && !failed) {
+    tsum += __shfl_xor_sync(kFull, tsum, 16);  // both halves' steps
+    const bool last = seg == a.nseg - 1;
+    if (nagg) {  // publish the aggregate (the last segment's is already inclusive)
+      float* dst = (last ? a.segI : a.segF) + (seg_row * Dm + c) * kN;
+      if (cvalid) {
+        *reinterpret_cast<float4*>(dst + q0) = make_float4(fa[0].x, fa[0].y, fa[1].x, fa[1].y);
+        *reinterpret_cast<float4*>(dst + (q0 ^ 4)) = make_float4(fa[2].x, fa[2].y, fa[3].x, fa[3].y);
+        if (hs == 0) a.segT[seg_row * Dm + c] = tsum;
+      }
+      __threadfence();
+      __syncthreads();
+      if (threadIdx.x == 0) st_release_gpu(my_flag, last ? kInclReady : kAggReady);
+    }
+    if (last) {  // nothing enters the last segment: its main pass starts from zero
+#pragma unroll
+      for (int p = 0; p < 4; ++p) fa[p] = make_float2(0.f, 0.f);
+    }
+    if (!last) {
+      // fold the published carries of the later segments: carry entering this
+      // segment = sum_s' exp(A * sum of dt of the segments between) * X_s',
+      // X the aggregate, or the inclusive carry (which ends the walk)
+      float2 carry[4];
+#pragma unroll
+      for (int p = 0; p < 4; ++p) carry[p] = make_float2(0.f, 0.f);
+      float tacc = 0.f;
+      for (int sp = seg + 1; sp < a.nseg; ++sp) {
+        const int f = cta_wait_flag(my_flag + (sp - seg), P.spin_limit, wait_slot);
+        if (f == 0) {
+          failed = true;
+          break;
+        }
+        const size_t row = ((size_t)b * a.nseg + sp) * Dm + (cvalid ? c : 0);
+        float2 X[4];
+        {
+          const float* src = (f == kInclReady ? a.segI : a.segF) + row * kN;
+          const float4 x0 = __ldcg(reinterpret_cast<const float4*>(src + q0));
+          const float4 x1 = __ldcg(reinterpret_cast<const float4*>(src + (q0 ^ 4)));
+          X[0] = make_float2(x0.x, x0.y);
+          X[1] = make_float2(x0.z, x0.w);
+          X[2] = make_float2(x1.x, x1.y);
+          X[3] = make_float2(x1.z, x1.w);
+        }
+        const float2 t2 = dup2(tacc);
+#pragma unroll
+        for (int p = 0; p < 4; ++p) {
+          const float2 e = fmul2(A2[p], t2);
+          carry[p] = ffma2(make_float2(ex2(e.x), ex2(e.y)), X[p], carry[p]);
+        }
+        if (f == kInclReady) break;
+        tacc += __ldcg(a.segT + row);
+      }
+      if (!failed && seg > 0) {  // publish the inclusive carry: F + exp(A T) carry
+        const float2 t2 = dup2(tsum);
+        float2 I[4];
+#pragma unroll
+        for (int p = 0; p < 4; ++p) {
+          const float2 e = fmul2(A2[p], t2);
+          I[p] = ffma2(make_float2(ex2(e.x), ex2(e.y)), carry[p], fa[p]);
+        }
+        if (cvalid) {
+          float* dst = a.segI + (seg_row * Dm + c) * kN;
+          *reinterpret_cast<float4*>(dst + q0) = make_float4(I[0].x, I[0].y, I[1].x, I[1].y);
+          *reinterpret_cast<float4*>(dst + (q0 ^ 4)) = make_float4(I[2].x, I[2].y, I[3].x, I[3].y);
+        }
+        __threadfence();
+        __syncthreads();
+        if (threadIdx.x == 0) st_release_gpu(my_flag, kInclReady);
+      }
+#pragma unroll
+      for (int p = 0; p < 4; ++p) fa[p] = carry[p];  // the main pass starts from the true carry
+    }
+  }
+
+  for (int it = 0; it < nloc && !failed; ++it) {
     const int j = j1 - 1 - it;
-    const int s = it % kBStages;
-    const bool ok = mbar_wait_bounded(&bars[s], (it / kBStages) & 1);
+    const int g = nagg + it;
+    const int s = g % kBStages;
+    const bool ok = mbar_wait_bounded(&bars[s], (g / kBStages) & 1);
     if (!__syncthreads_and(ok)) {
       failed = true;
       break;
@@ -456,9 +609,9 @@ __global__ void __launch_bounds__(kBThreads, 2) ssm_bwd_kernel(const __grid_cons
     }
 
     __syncthreads();  // stage s consumed; red[] complete
-    if (threadIdx.x == 0 && it + kBStages < nloc) {
+    if (threadIdx.x == 0 && g + kBStages < ntot) {
       fence_proxy_async_smem();
-      issue(it + kBStages);
+      issue(g + kBStages);
     }
     if (threadIdx.x < kChunk * 8) {
       // sum the 8 warps' partials: thread -> (step, 4 consecutive outputs)
@@ -475,7 +628,7 @@ __global__ void __launch_bounds__(kBThreads, 2) ssm_bwd_kernel(const __grid_cons
           float* dst = (q4 < 4 ? a.dB_acc : a.dC_acc) + ((size_t)b * L + t) * a.acc_stride + (q4 & 3) * 4;
           multimem_red_add4(dst, v);
         } else {  // this tile's partial; finalize sums the tiles in order
-          *reinterpret_cast<float4*>(a.bc_part + (((size_t)blockIdx.x * gridDim.y + b) * L + t) * 32 + q4 * 4) = v;
+          *reinterpret_cast<float4*>(a.bc_part + (((size_t)tile * P.batch + b) * L + t) * 32 + q4 * 4) = v;
         }
       }
     }
@@ -501,134 +654,6 @@ __global__ void __launch_bounds__(kBThreads, 2) ssm_bwd_kernel(const __grid_cons
       a.dD_part[r * Dm + c] = dD_acc;
       a.db_part[r * Dm + c] = db_acc;
     }
-  }
-}
-
-// Backward segment pre-pass: for segment s >= 1 runs the adjoint recurrence
-// f_t = C_t dy_t + f_{t+1} alpha_{t+1} over the segment from a zero carry and
-// writes the carry leaving its first step (f alpha, natural state order) and
-// the segment's sum of dt.  Reads delta, C, dout and z only.
-// State pairs per lane whose exponential the pre-pass evaluates on the FMA
-// pipe (ex2_poly2): the pre-pass is otherwise bound by the MUFU unit.
-constexpr int kAggEmu = 1;
-
-struct BwdAggLayout {
-  int offDelta, offDo, offZo, offC, stage, offBars, bytes;
-  __host__ __device__ BwdAggLayout(int es, int esbc, bool has_z) {
-    const int act = kChunk * kBTile * es, bc = kChunk * kN * esbc;
-    int o = 0;
-    offDelta = o; o += act;
-    offDo = o; o += act;
-    offZo = o; if (has_z) o += act;
-    offC = o; o += bc;
-    stage = (o + 127) & ~127;
-    offBars = stage * kBStages;
-    bytes = offBars + 8 * kBStages;
-  }
-};
-
-template <typename T, typename TBC, int G>
-__global__ void __launch_bounds__(kAggThreads, 4) ssm_bwd_agg_kernel(const __grid_constant__ BwdLaunch P) {
-  const BwdDir& a = P.dir[blockIdx.z / P.zdiv];
-  const int seg = 1 + blockIdx.z % P.zdiv;  // segments 1 .. nseg-1
-  extern __shared__ __align__(1024) unsigned char smem[];
-  const int b = blockIdx.y;
-  const int c0 = blockIdx.x * kBTile;
-  const int cl = threadIdx.x;
-  const int c = c0 + cl;
-  const int L = a.L, Dm = a.Dm;
-  if (c0 >= Dm) return;
-  const bool rev = (a.flags & SSM_REVERSE) != 0;
-  const bool comp = rev && (a.flags & SSM_COMPLEMENT);
-  const bool softplus = (a.flags & SSM_DELTA_SOFTPLUS) != 0;
-  const bool has_z = a.has_z != 0;
-  const int nblk = (L + kChunk - 1) / kChunk;
-  const int j1 = min(nblk, (seg + 1) * a.seg_chunks);
-  const int nloc = j1 - seg * a.seg_chunks;
-  const bool cvalid = c < Dm;
-  const int oc0 = comp ? Dm - kBTile - c0 : c0;
-  const int col = comp ? kBTile - 1 - cl : cl;
-  const BwdAggLayout S(sizeof(T), sizeof(TBC), has_z);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S.offBars);
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < kBStages; ++s) mbar_init(&bars[s], 1);
-    fence_mbar_init();
-  }
-  __syncthreads();
-  const uint32_t tx = (2 + (has_z ? 1 : 0)) * kChunk * kBTile * (int)sizeof(T) + kChunk * kN * (int)sizeof(TBC);
-  auto issue = [&](int it) {
-    const int j = j1 - 1 - it;
-    unsigned char* st = smem + (it % kBStages) * S.stage;
-    uint64_t* bar = &bars[it % kBStages];
-    const int t0 = j * kChunk;
-    const int ot0 = rev ? L - kChunk - t0 : t0;
-    mbar_arrive_expect_tx(bar, tx);
-    tma_load_3d(st + S.offDelta, &a.tm_delta, bar, c0, t0, b);
-    tma_load_3d(st + S.offC, &a.tm_C, bar, 0, t0, b);
-    tma_load_3d(st + S.offDo, &a.tm_dout, bar, oc0, ot0, b);
-    if (has_z) tma_load_3d(st + S.offZo, &a.tm_z, bar, oc0, ot0, b);
-  };
-  if (threadIdx.x == 0) {
-    const int npre = nloc < kBStages ? nloc : kBStages;
-    for (int it = 0; it < npre; ++it) issue(it);
-  }
-  float2 A2[8];
-  {
-    const float* Ar = a.A + (size_t)(cvalid ? c : 0) * kN;
-#pragma unroll
-    for (int p = 0; p < 8; ++p)
-      A2[p] = cvalid ? make_float2(Ar[2 * p] * kLog2e, Ar[2 * p + 1] * kLog2e) : make_float2(0.f, 0.f);
-  }
-  const float bias = (a.bias && cvalid) ? a.bias[c] : 0.f;
-  float2 fa[8];
-#pragma unroll
-  for (int p = 0; p < 8; ++p) fa[p] = make_float2(0.f, 0.f);
-  float tsum = 0.f;
-  for (int it = 0; it < nloc; ++it) {
-    const int j = j1 - 1 - it;
-    const int s = it % kBStages;
-    const bool ok = mbar_wait_bounded(&bars[s], (it / kBStages) & 1);
-    if (!__syncthreads_and(ok)) {
-      if (threadIdx.x == 0) report(a.status, kStatusTimeout);
-      return;
-    }
-    const unsigned char* st = smem + s * S.stage;
-    const T* sd = reinterpret_cast<const T*>(st + S.offDelta) + cl;
-    const T* sdo = reinterpret_cast<const T*>(st + S.offDo) + col;
-    const T* szo = reinterpret_cast<const T*>(st + S.offZo) + col;
-    const TBC* sC = reinterpret_cast<const TBC*>(st + S.offC);
-#pragma unroll
-    for (int tl = kChunk - 1; tl >= 0; --tl) {
-      const bool valid = j * kChunk + tl < L;
-      const float dr = ld_f(sd + tl * kBTile) + bias;
-      float dt = softplus ? softplus_f(dr) : dr;
-      dt = valid ? dt : 0.f;
-      tsum += dt;
-      const int row = rev ? kChunk - 1 - tl : tl;
-      float g = ld_f(sdo + row * kBTile);
-      if (has_z) g *= act_f(ld_f(szo + row * kBTile), G);
-      const float2 dy2 = dup2(valid ? g : 0.f), dt2 = dup2(dt);
-      float2 Cq[8];
-      ld16(sC + tl * kN, Cq);
-#pragma unroll
-      for (int p = 0; p < 8; ++p) {
-        const float2 e = fmul2(A2[p], dt2);
-        const float2 al = p < kAggEmu ? ex2_poly2(e) : make_float2(ex2(e.x), ex2(e.y));
-        fa[p] = fmul2(ffma2(Cq[p], dy2, fa[p]), al);
-      }
-    }
-    __syncthreads();
-    if (threadIdx.x == 0 && it + kBStages < nloc) {
-      fence_proxy_async_smem();
-      issue(it + kBStages);
-    }
-  }
-  if (cvalid) {
-    const size_t r = (size_t)b * a.nseg + seg;
-    float4* F = reinterpret_cast<float4*>(a.segF + (r * Dm + c) * kN);
-#pragma unroll
-    for (int q = 0; q < 4; ++q) F[q] = make_float4(fa[2 * q].x, fa[2 * q].y, fa[2 * q + 1].x, fa[2 * q + 1].y);
-    a.segT[r * Dm + c] = tsum;
   }
 }
 

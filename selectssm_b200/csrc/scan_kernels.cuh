@@ -1,12 +1,13 @@
 // Selective-scan launch arguments shared by the forward (scan_fwd.cuh) and
-// backward (scan_bwd.cuh) kernels, the backward segment fold and the
-// finalize step.
+// backward (scan_bwd.cuh) kernels and the finalize step, and the decoupled
+// lookback helpers.
 //
 // Segments: when there are too few (batch row, channel tile) chains to fill
-// the GPU the sequence is cut into segments that run as separate CTAs.  A
-// pre-pass computes each segment's end state (forward) or the adjoint carried
-// out of its first step (backward) from a zero start, plus its sum of dt; the
-// main pass folds those of the neighbouring segments into its start state.
+// the GPU the sequence is cut into segments that run as separate CTAs.  The
+// forward's pre-pass computes each segment's end state from a zero start plus
+// its sum of dt and the main pass folds those of the preceding segments into
+// its start state; the backward does the same for the adjoint inside one
+// launch, with flags (decoupled lookback).
 #pragma once
 
 #include "common.cuh"
@@ -54,6 +55,8 @@ struct BwdDir {
   float* db_part;  // (B, nseg, D)
   float* segF;     // (B, nseg, D, 16) adjoint carried out of each segment's first step, zero start
   float* segT;     // (B, nseg, D) sum of dt over each segment
+  float* segI;     // (B, nseg, D, 16) adjoint carried out of each segment's first step, true start
+  int* seg_flag;   // (B, channel tiles, nseg) lookback flags: kAggReady / kInclReady
   int32_t* status;
   int64_t z_stride, acc_stride;
   int L, Dm, flags, gate_act, has_z;
@@ -66,47 +69,56 @@ constexpr int kBcMulticast = 1;  // multimem.red at dB_acc / dC_acc (NVLink mult
 struct BwdLaunch {
   BwdDir dir[2];
   int zdiv;
+  int* ticket;       // CTA order counter (zeroed per call); null when nothing is segmented
+  int ticket_base;   // added to every ticket (0; the lookback self-test skips the last segment)
+  int chains;        // CTAs per segment: channel tiles x batch rows x directions
+  int ntile, batch;
+  uint32_t spin_limit;  // polls of a lookback flag before giving up
 };
+
+// ---------------------------------------------------------------- decoupled lookback
+// Segments of one chain publish, per channel, their zero-start aggregate
+// (flag kAggReady) and later their inclusive carry (flag kInclReady); a CTA
+// folds the published values of the segments before it (in scan order) until
+// it meets an inclusive one.  CTAs take their segment from an atomic ticket in
+// scan order, so every segment a CTA waits for belongs to a CTA that is
+// already resident or finished.
+constexpr int kAggReady = 1;
+constexpr int kInclReady = 2;
+constexpr uint32_t kLookbackSpin = 1u << 22;  // polls (each sleeps ~0.1 us): seconds, far above any real wait
+
+__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_gpu(int* p, int v) {
+  asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+// Polls *flag until it is non-zero; returns its value, or 0 after `limit` polls.
+__device__ __forceinline__ int wait_flag_bounded(const int* flag, uint32_t limit) {
+  for (uint32_t i = 0; i < limit; ++i) {
+    const int v = ld_acquire_gpu(flag);
+    if (v) return v;
+    __nanosleep(100);
+  }
+  return 0;
+}
+// CTA-wide wait: thread 0 polls, the result is broadcast through `slot`, and
+// every thread then re-reads the flag with acquire semantics so its own later
+// loads of the published values are ordered after the publisher's stores.
+__device__ __forceinline__ int cta_wait_flag(const int* flag, uint32_t limit, int* slot) {
+  if (threadIdx.x == 0) *slot = wait_flag_bounded(flag, limit);
+  __syncthreads();
+  const int v = *slot;
+  __syncthreads();
+  if (v) (void)ld_acquire_gpu(flag);
+  return v;
+}
 
 template <typename T>
 __device__ __forceinline__ void st_act(T* p, float v) {
   *p = Cvt<T>::from_f(v);
-}
-
-// Turns the per-segment adjoint aggregates into the adjoint entering each
-// segment from the right, in place: carry_{S-1} = 0,
-// carry_s = exp(A T_{s+1}) carry_{s+1} + F_{s+1}.  One thread per (b, d, n).
-// The loads of a batch of 8 segments are issued before the dependent chain
-// runs through them, so the chain waits on one load latency per batch.
-// Grid: (channel*state blocks, direction, batch row).
-__global__ void ssm_bwd_fold_kernel(const __grid_constant__ BwdLaunch P) {
-  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  const BwdDir& a = P.dir[blockIdx.y];
-  if (i >= (int64_t)a.Dm * kN) return;
-  const int b = blockIdx.z;
-  const int c = (int)(i / kN), n = (int)(i % kN);
-  const float A2 = a.A[(size_t)c * kN + n] * kLog2e;
-  const size_t row0 = (size_t)b * a.nseg;
-  float carry = 0.f;
-  constexpr int kBatch = 8;
-  for (int top = a.nseg - 1; top >= 0; top -= kBatch) {
-    float F[kBatch], T[kBatch];
-#pragma unroll
-    for (int k = 0; k < kBatch; ++k) {
-      const int sg = top - k;
-      const size_t r = row0 + (sg > 0 ? sg : 0);
-      F[k] = sg > 0 ? a.segF[(r * a.Dm + c) * kN + n] : 0.f;
-      T[k] = sg > 0 ? a.segT[r * a.Dm + c] : 0.f;
-    }
-#pragma unroll
-    for (int k = 0; k < kBatch; ++k) {
-      const int sg = top - k;
-      if (sg >= 0) {
-        a.segF[((row0 + sg) * a.Dm + c) * kN + n] = carry;
-        carry = fmaf(ex2(A2 * T[k]), carry, F[k]);
-      }
-    }
-  }
 }
 
 // Sums the per-(batch row, segment) partials of dA / dD / d(bias) in row order
