@@ -1,20 +1,22 @@
 """Benchmark of the selectssm selective-scan hot path on B200.
 
-Metric: scan fwd+bwd tokens*channels/s and % of the HBM roofline.
-Workload at N=1: config 2 of the benchmark contract -- the raw selective-scan op
-forward + backward in float32, batch=8, L=4096, d_inner=1536, N=16, with the
-softplus(dt) preamble, D skip and silu(z) gate fused in; synthetic seeded inputs
-(u, z ~ N(0,1); dt_raw ~ N(0,1) - 4; A = -U[1,16]; B, C ~ N(0,1); D ~ N(1, 0.1);
-upstream grad ~ N(0,1)).  One step = one forward + one backward over the batch.
-
-Multi-GPU (torchrun, one process per GPU): weak scaling, each rank scans its own
-batch of 8 sequences (batch sharding, no collective in the forward) and the
-backward ends with one NCCL all-reduce of the small parameter gradients
-(dA, dD) -- the only exchange the partition needs.
+Metric: scan fwd+bwd tokens*channels/s and % of the HBM roofline
+at 1/2/4/8 B200.  Headline workload at every N: config 5 of the benchmark
+contract, the raw selective-scan op forward + backward (softplus(dt) preamble,
+D skip and silu(z) gate fused) on batch=64, L=2048, d_inner=1536, N=16 with
+bf16 I/O and fp32 state, the batch split over the N ranks (strong scaling: the
+total problem is fixed).  Synthetic seeded inputs with config 2's distributions
+(u, z ~ N(0,1); dt_raw ~ N(0,1) - 4; A = -U[1,16]; B, C ~ N(0,1);
+D ~ N(1, 0.1); upstream grad ~ N(0,1)).  One step = one forward + one backward.
+At N=1 the line also carries config 2 (batch=8, L=4096, float32) under
+"config2".  Multi-GPU: one process per GPU (torchrun), no collective in the
+forward, one NCCL all-reduce of dA / dD per backward, overlapped with the next
+forward.  --parallel channels splits d_inner instead (config 4 with
+--workload 4) and sums dB / dC over the ranks.
 
 `--impl reference` times the reference algorithm on the host CPU instead: the
 NumPy restatement of ssm_chunked_scan (forward) and of the ssm_scan custom-VJP
-backward from oracle/, on a bounded prefix of the same workload (JAX, the
+backward from oracle/, on a bounded sample of the same workload (JAX, the
 reference's own runtime, is not installed on this image).
 """
 
@@ -244,22 +246,24 @@ def _run_shard(span):
 
 class CpuSampler:
     """Times the NumPy restatement of the reference algorithm on all host
-    cores: the channels of one fixed sample are split over one single-threaded
-    process per core (the reference's JAX-on-CPU would also use every core).
-    The workers are forked after the sample is drawn, so they share it."""
+    cores: the channels of one fixed sample of the workload are split over one
+    single-threaded process per core (the reference's JAX-on-CPU would also use
+    every core).  The workers are forked after the sample is drawn, so they
+    share it.  The sample is float32 (for a bf16 workload the oracle computes
+    in float32 on the same distributions)."""
 
-    def __init__(self, seqlen, batch=1):
+    def __init__(self, spec, seqlen, batch=1):
         import multiprocessing as mp
         global _SAMPLE_INP
-        D, N = CFG["dim"], CFG["dstate"]
+        D, N = spec["dim"], CFG["dstate"]
         _SAMPLE_INP = host_inputs(0, batch, seqlen, D, N)
         self.procs = cpu_cores()
         k = self.procs
         self.spans = [(D * i // k, D * (i + 1) // k) for i in range(k)]
         self.units = batch * seqlen * D
         self.sample = (f"NumPy restatement of the reference algorithm (chunked scan fwd + custom-VJP bwd, float32) "
-                       f"on batch={batch}, L={seqlen}, d_inner={D}, N={N} of the config-2 workload, channels split "
-                       f"over {k} single-threaded processes (one per host core), after one warm-up run")
+                       f"on batch={batch}, L={seqlen}, d_inner={D}, N={N} of the {spec['key']} workload, channels "
+                       f"split over {k} single-threaded processes (one per host core), after one warm-up run")
         self.pool = mp.get_context("fork").Pool(k, initializer=_one_thread)
         self.pool.map(_run_shard, self.spans)  # warm-up (imports, page faults)
 
@@ -274,8 +278,8 @@ class CpuSampler:
         self.pool.join()
 
 
-def run_cpu_sample(seqlen=4096, batch=1):
-    sampler = CpuSampler(seqlen, batch)
+def run_cpu_sample(spec, seqlen, batch=1):
+    sampler = CpuSampler(spec, seqlen, batch)
     try:
         return sampler.run()
     finally:
@@ -387,114 +391,89 @@ def run_other_config(args):
 
 
 # ----------------------------------------------------------------------------- GPU arm
-def main():
-    ap = argparse.ArgumentParser()
-    ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=1000)
-    ap.add_argument("--warmup", type=int, default=10)
-    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--e2e-steps", type=int, default=20)
-    ap.add_argument("--batch", type=int, default=None, help="override batch per GPU (small profiling cases)")
-    ap.add_argument("--config", type=int, default=2, choices=[2, 3, 4, 5],
-                    help="2 (default) is the benchmark line; 3, 4 and 5 time the other contract workloads "
-                         "device-resident on one GPU (no e2e or CPU legs)")
-    ap.add_argument("--parallel", default="batch", choices=["batch", "channels"],
-                    help="N>1 sharding: batch rows (default) or d_inner channels with B/C replicated")
-    ap.add_argument("--bc-sum", default="multicast", choices=["multicast", "nccl"],
-                    help="channel sharding: sum dB/dC inside the backward kernel over NVLink multicast "
-                         "(default, when the GPUs support it) or with an NCCL all-reduce after it")
-    args = ap.parse_args()
+# Workloads of the GPU arm.  The headline (every N) is config 5, the contract's
+# scaling workload: the batch of 64 sequences is split over the N ranks, so the
+# total problem is fixed (strong scaling).  At N=1 the line also carries config
+# 2 (the raw op in float32) under "config2".  With --parallel channels the
+# d_inner channels are split instead (config 4: 8 x 128 channels), B and C are
+# replicated and dB / dC are summed over the ranks.
+SPECS = {
+    5: dict(key="config5", workload="config 5: raw selective-scan op fwd+bwd (softplus dt, D skip, silu gate "
+                                    "fused), bf16 I/O, fp32 state", batch=64, seqlen=2048, dim=1536, dtype="bf16"),
+    2: dict(key="config2", workload="config 2: raw selective-scan op fwd+bwd (softplus dt, D skip, silu gate "
+                                    "fused), fp32", batch=8, seqlen=4096, dim=1536, dtype="f32"),
+    4: dict(key="config4", workload="config 4: long-sequence raw op fwd+bwd (recursive-scan semantics), fp32",
+            batch=1, seqlen=1 << 20, dim=1024, dtype="f32"),
+}
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
-    if args.config != 2:
-        if world != 1 or args.impl != "ours":
-            raise SystemExit("--config 3/4/5 time one GPU with the CUDA path only")
-        return run_other_config(args)
-    if args.batch:
-        CFG["batch"] = args.batch
-    Bsz, L, D, N = CFG["batch"], CFG["seqlen"], CFG["dim"], CFG["dstate"]
-    config = {"workload": "config 2: raw selective-scan op fwd+bwd (softplus dt, D skip, silu gate fused)",
-              "batch_per_gpu": Bsz, "global_batch": Bsz * world, "seq_len": L, "d_inner": D, "d_state": N,
-              "parallelism": ("single GPU" if world == 1 else
-                              f"batch-sharded dp{world}, NCCL all-reduce of dA/dD in bwd" if args.parallel == "batch"
-                              else f"d_inner-sharded x{world} ({D} channels per GPU), B/C replicated, dB/dC"),
-              "l2": "inputs larger than L2 (u, dt, z, dy = 805 MB per step), no flush"}
 
-    if args.impl == "reference":
-        if rank != 0:
-            return
-        steps = max(1, args.steps)
-        vals = []
-        # each step times the oracle on one full-width batch row of L=256, split
-        # over all host cores (about 0.1 s), so 1000 steps stay within minutes
-        sampler = CpuSampler(256)
-        for _ in range(args.warmup):
-            sampler.run()
-        t0 = time.perf_counter()
-        for _ in range(steps):
-            v, _, sample = sampler.run()
-            vals.append(v)
-        sampler.close()
-        total = time.perf_counter() - t0
-        v = statistics.median(vals)
-        line = {"metric": METRIC, "value": v, "unit": UNIT, "n_gpus": world, "steps": steps,
-                "warmup": args.warmup, "ms_per_step": 1e3 * total / steps, "higher_is_better": True,
-                "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": config,
-                "impl": "reference",
-                "cpu_baseline": {"value": v, "unit": UNIT, "cores": cpu_cores(), "kind": "port",
-                                 "sample": sample},
-                "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
-        print(json.dumps(line))
-        return
+def device_inputs(spec, batch, dim, seed, bc_seed, dev):
+    """Seeded inputs on the device with config 2's distributions (u, z ~ N(0,1);
+    dt_raw ~ N(0,1) - 4; A = -U[1,16]; B, C ~ N(0,1); D ~ N(1, 0.1); upstream
+    grad ~ N(0,1)), in the workload's dtype.  B and C come from bc_seed (shared
+    by channel shards)."""
+    import torch
+    dt = torch.bfloat16 if spec["dtype"] == "bf16" else torch.float32
+    L, N = spec["seqlen"], CFG["dstate"]
+    g = torch.Generator(device=dev).manual_seed(seed)
+    gb = torch.Generator(device=dev).manual_seed(bc_seed)
+    n = lambda gen, *s: torch.randn(*s, generator=gen, device=dev)  # noqa: E731
+    t = {"u": n(g, batch, L, dim).to(dt), "delta": (n(g, batch, L, dim) - 4.0).to(dt), "z": n(g, batch, L, dim).to(dt),
+         "A": -(1.0 + 15.0 * torch.rand(dim, N, generator=g, device=dev)),
+         "B": n(gb, batch, L, N).to(dt), "C": n(gb, batch, L, N).to(dt),
+         "D": 1.0 + 0.1 * n(g, dim), "dout": n(g, batch, L, dim).to(dt)}
+    return t
 
+
+GRAD_KEYS = ("u", "delta", "z", "A", "B", "C", "D")
+
+
+def measure(spec, args, world, rank, dev, lib, chan=False, bc_sum_mode="multicast", e2e=True):
+    """Times one workload on this rank: `steps` fwd+bwd steps device-resident
+    (CUDA events, max over ranks), the per-call forward / backward split, and
+    the same steps end to end from pinned host buffers.  Returns the fields of
+    the JSON line."""
     import torch
     import torch.distributed as dist
     import selectssm_b200 as S
-    from selectssm_b200 import _lib
     from selectssm_b200.parallel import MulticastBCSum, allreduce_grads, replicated_bc
 
-    torch.cuda.set_device(local_rank)
-    dev = torch.device("cuda", local_rank)
-    if world > 1:
-        dist.init_process_group("nccl", device_id=dev)
-    lib = _lib.load()
-
-    chan = world > 1 and args.parallel == "channels"
-    h = host_inputs(1234 + rank, Bsz, L, D, N, bc_seed=1234 if chan else None)
-    t = {k: torch.from_numpy(v).to(dev) for k, v in h.items()}
-    for k in ("u", "delta", "z", "A", "B", "C", "D"):
+    N = CFG["dstate"]
+    L = spec["seqlen"]
+    if chan:
+        Bsz, D = spec["batch"], spec["dim"] // world
+    else:
+        Bsz, D = spec["batch"] // world, spec["dim"]
+    if args.batch:
+        Bsz = args.batch
+    t = device_inputs(spec, Bsz, D, 1234 + rank, 1234 if chan else 1234 + rank, dev)
+    for k in GRAD_KEYS:
         t[k].requires_grad_(True)
-
+    s = t["u"].element_size()
     pending = []
     bcs = None
-    if chan and args.bc_sum == "multicast":
+    if chan and bc_sum_mode == "multicast":
         bcs = MulticastBCSum(Bsz, L, device=dev)
         if not bcs.available:
             bcs = None
-    if chan:
-        config["parallelism"] += (" summed inside the backward kernel by NVLink multicast (multimem.red)" if bcs
-                                  else " summed by an NCCL all-reduce after the backward")
+
+    def finish_reduce():
+        while pending:
+            pending.pop().wait()
 
     def step(inputs):
-        for k in ("u", "delta", "z", "A", "B", "C", "D"):
+        for k in GRAD_KEYS:
             inputs[k].grad = None
         Bm, Cm = inputs["B"], inputs["C"]
-        if chan and bcs is None:  # channel sharding: the B / C gradients are summed over ranks in the backward
+        if chan and bcs is None:  # dB / dC summed over the channel shards by NCCL after the backward
             Bm, Cm = replicated_bc(Bm, Cm)
-        out = S.selective_scan(inputs["u"], inputs["delta"], inputs["A"], Bm, Cm, D=inputs["D"],
-                               z=inputs["z"], delta_softplus=True, bc_sum=bcs)
+        out = S.selective_scan(inputs["u"], inputs["delta"], inputs["A"], Bm, Cm, D=inputs["D"], z=inputs["z"],
+                               delta_softplus=True, bc_sum=bcs)
         out.backward(inputs["dout"])
         if world > 1 and not chan:  # batch sharding: one all-reduce of the parameter gradients,
             finish_reduce()            # overlapped with the next step's forward
             pending.append(allreduce_grads([inputs["A"], inputs["D"]], async_op=True))
         return out
-
-    def finish_reduce():
-        while pending:
-            pending.pop().wait()
 
     for _ in range(max(3, args.warmup)):
         step(t)
@@ -505,7 +484,7 @@ def main():
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
-    with ClockSampler(local_rank) as clk:
+    with ClockSampler(dev.index) as clk:
         clk.wait_first()
         n_launch0 = lib.ssm_launch_count()
         e0.record(stream)
@@ -521,54 +500,59 @@ def main():
         dist.all_reduce(mt, op=dist.ReduceOp.MAX)
         ms = float(mt.item())
         dist.barrier()
-
-    units = Bsz * L * D
+    units = Bsz * L * D  # per rank
     value = units * world / (ms * 1e-3)
 
-    # --- per-call timing of the forward and backward (same stream).  The calls
-    # are queued back to back, as in the training loop, so host-side overhead
-    # overlaps the GPU work and the events time the kernels.
-    p_fwd, p_bwd = [], []
+    # per-call forward / backward times, calls queued back to back as in training
     marks = []
     torch.cuda.synchronize()
     for _ in range(8):
-        a0, a1, a2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
-        for k in ("u", "delta", "z", "A", "B", "C", "D"):
+        a = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+        for k in GRAD_KEYS:
             t[k].grad = None
-        a0.record(stream)
-        out = S.selective_scan(t["u"], t["delta"], t["A"], t["B"], t["C"], D=t["D"], z=t["z"], delta_softplus=True)
-        a1.record(stream)
+        a[0].record(stream)
+        out = S.selective_scan(t["u"], t["delta"], t["A"], t["B"], t["C"], D=t["D"], z=t["z"], delta_softplus=True,
+                               bc_sum=bcs)
+        a[1].record(stream)
         out.backward(t["dout"])
-        a2.record(stream)
-        marks.append((a0, a1, a2))
+        a[2].record(stream)
+        marks.append(a)
     torch.cuda.synchronize()
-    for a0, a1, a2 in marks[1:]:
-        p_fwd.append(a0.elapsed_time(a1))
-        p_bwd.append(a1.elapsed_time(a2))
-    t_fwd, t_bwd = statistics.median(p_fwd), statistics.median(p_bwd)
+    t_fwd = statistics.median(a[0].elapsed_time(a[1]) for a in marks[1:])
+    t_bwd = statistics.median(a[1].elapsed_time(a[2]) for a in marks[1:])
     hbm, src = peaks()
-    fb, bb = alg_bytes(units, 4, N, D)
-    roof_bwd = {"kernel": "ssm_bwd call: ssm_bwd_kernel<float,float> + segment pre-pass, fold, zero, finalize", "bound": "hbm",
-                "achieved": bb / (t_bwd * 1e-3) / 1e9, "peak": hbm, "unit": "GB/s", "peak_source": src,
-                "traffic": read_traffic("ssm_bwd_kernel_config2.md"), "algorithmic_bytes": bb,
-                "ms": t_bwd}
+    fb, bb = alg_bytes(units, s, N, D)
+    roof_bwd = {"kernel": "ssm_bwd call: ssm_bwd_kernel (decoupled-lookback segments) + finalize_kernel",
+                "bound": "hbm", "achieved": bb / (t_bwd * 1e-3) / 1e9, "peak": hbm, "peak_source": src,
+                "unit": "GB/s", "traffic": read_traffic(f"ssm_bwd_kernel_{spec['key']}.md"),
+                "algorithmic_bytes": bb, "ms": t_bwd}
     roof_bwd["frac"] = roof_bwd["achieved"] / hbm
-    roof_fwd = {"kernel": "ssm_fwd call: ssm_fwd_kernel<float,float,0,1> (+ segment pre-pass when segmented)", "bound": "hbm", "achieved": fb / (t_fwd * 1e-3) / 1e9,
-                "peak": hbm, "unit": "GB/s", "traffic": read_traffic("ssm_fwd_kernel_config2.md"),
-                "algorithmic_bytes": fb, "ms": t_fwd}
+    roof_fwd = {"kernel": "ssm_fwd call: ssm_fwd_kernel (+ segment pre-pass when segmented)", "bound": "hbm",
+                "achieved": fb / (t_fwd * 1e-3) / 1e9, "peak": hbm, "peak_source": src, "unit": "GB/s",
+                "traffic": read_traffic(f"ssm_fwd_kernel_{spec['key']}.md"), "algorithmic_bytes": fb, "ms": t_fwd}
     roof_fwd["frac"] = roof_fwd["achieved"] / hbm
-    step_roof = {"achieved": (fb + bb) / (ms * 1e-3) / 1e9, "peak": hbm, "unit": "GB/s"}
+    step_roof = {"achieved": (fb + bb) / (ms * 1e-3) / 1e9, "peak": hbm, "peak_source": src, "unit": "GB/s",
+                 "bytes_per_unit": (fb + bb) / units}
     step_roof["frac"] = step_roof["achieved"] / hbm
+    res = {"value": value, "ms_per_step": ms, "units_per_rank": units, "batch_per_gpu": Bsz, "d_inner_per_gpu": D,
+           "roofline": roof_bwd, "roofline_fwd": roof_fwd, "roofline_step": step_roof,
+           "gpu_launches": n_launches, "clocks": clk.summary(), "dtype": spec["dtype"]}
+    if e2e:
+        res["e2e"] = measure_e2e(t, step, stream, world, args, units, dev, finish_reduce)
+    return res
 
-    # --- end to end through the public API: pinned host inputs -> device, fwd+bwd,
-    # outputs and gradients -> pinned host
-    # Pipelined over steps on three streams: the upload of step i+1 (copy_in)
-    # and the download of step i-1 (copy_out) overlap the compute of step i;
-    # every step still moves all of its inputs and results across PCIe.
-    pin = {k: torch.from_numpy(v).pin_memory() for k, v in h.items()}
+
+def measure_e2e(t, step, stream, world, args, units, dev, finish_reduce):
+    """The same steps through the public API with host buffers: every step
+    uploads its inputs from pinned host memory and downloads the output and
+    all gradients to pinned host memory, inside the timed region.  Pipelined
+    over steps on two copy streams (upload of step i+1 and download of step i-1
+    overlap the compute of step i)."""
+    import torch
+    import torch.distributed as dist
+    pin = {k: v.detach().cpu().pin_memory() for k, v in t.items()}
     h2d = sum(v.numel() * v.element_size() for v in pin.values())
-    grad_keys = ("u", "delta", "z", "A", "B", "C", "D")
-    slots = [{k: torch.empty(v.shape, dtype=v.dtype, device=dev).requires_grad_(k in grad_keys)
+    slots = [{k: torch.empty(v.shape, dtype=v.dtype, device=dev).requires_grad_(k in GRAD_KEYS)
               for k, v in pin.items()} for _ in range(2)]
     copy_in, copy_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
     ev_in = [torch.cuda.Event() for _ in range(2)]
@@ -586,7 +570,7 @@ def main():
         s = i % 2
         stream.wait_event(ev_in[s])
         out = step(slots[s])
-        res = [out.detach()] + [slots[s][k].grad for k in grad_keys]
+        res = [out.detach()] + [slots[s][k].grad for k in GRAD_KEYS]
         ev_done[s].record(stream)
         if outs_host[s] is None:  # pinned result buffers, allocated before the timed region
             outs_host[s] = [torch.empty(r.shape, dtype=r.dtype, pin_memory=True) for r in res]
@@ -605,6 +589,7 @@ def main():
         stream.wait_stream(copy_out)
 
     pipeline(2)
+    finish_reduce()
     torch.cuda.synchronize()
     d2h = sum(r.numel() * r.element_size() for r in outs_host[0])
     ee0, ee1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -621,23 +606,121 @@ def main():
         mt = torch.tensor([ems], device=dev)
         dist.all_reduce(mt, op=dist.ReduceOp.MAX)
         ems = float(mt.item())
+    return {"value": units * world / (ems * 1e-3), "unit": UNIT, "h2d_bytes_per_step": h2d,
+            "d2h_bytes_per_step": d2h, "ms_per_step": ems, "path": "selectssm_b200.selective_scan, pinned host "
+            "buffers, copies inside the timed region"}
 
-    line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-            "warmup": max(3, args.warmup), "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": config,
-            "roofline": roof_bwd, "roofline_fwd": roof_fwd, "roofline_step": step_roof,
-            "e2e": {"value": units * world / (ems * 1e-3), "unit": UNIT, "h2d_bytes_per_step": h2d,
-                    "d2h_bytes_per_step": d2h, "ms_per_step": ems},
-            "gpu_launches": n_launches,
-            "clocks": clk.summary(), "library": lib.ssm_version().decode()}
+
+def config_of(spec, world, chan, res):
+    par = ("single GPU" if world == 1 else
+           f"d_inner-sharded x{world} ({res['d_inner_per_gpu']} channels per GPU), B/C replicated, dB/dC summed "
+           "over the ranks" if chan else
+           f"batch-sharded dp{world} ({res['batch_per_gpu']} sequences per GPU), one NCCL all-reduce of dA/dD "
+           "per backward, overlapped with the next forward")
+    return {"workload": spec["workload"], "global_batch": spec["batch"], "batch_per_gpu": res["batch_per_gpu"],
+            "seq_len": spec["seqlen"], "d_inner": spec["dim"], "d_inner_per_gpu": res["d_inner_per_gpu"],
+            "d_state": CFG["dstate"], "parallelism": par,
+            "l2": "inputs larger than L2 (u, dt, z, dy of every step exceed 126 MB), no flush"}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-config2", action="store_true", help="skip the config-2 keys at N=1")
+    ap.add_argument("--e2e-steps", type=int, default=10)
+    ap.add_argument("--batch", type=int, default=None, help="override batch per GPU (small profiling cases)")
+    ap.add_argument("--workload", type=int, default=5, choices=[2, 4, 5],
+                    help="5 (default): the scaling workload, batch of 64 split over the ranks; 2: config 2 alone; "
+                         "4: config 4 (with --parallel channels)")
+    ap.add_argument("--config", type=int, default=None, choices=[3, 4],
+                    help="time config 3 or 4 device-resident on one GPU (no e2e or CPU legs)")
+    ap.add_argument("--parallel", default="batch", choices=["batch", "channels"],
+                    help="N>1 sharding: batch rows (default) or d_inner channels with B/C replicated")
+    ap.add_argument("--bc-sum", default="multicast", choices=["multicast", "nccl"],
+                    help="channel sharding: sum dB/dC inside the backward kernel over NVLink multicast "
+                         "(default, when the GPUs support it) or with an NCCL all-reduce after it")
+    args = ap.parse_args()
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.config is not None:
+        if world != 1 or args.impl != "ours":
+            raise SystemExit("--config 3/4 time one GPU with the CUDA path only")
+        return run_other_config(args)
+    spec = SPECS[args.workload]
+    chan = args.parallel == "channels" and world > 1
+    if args.impl == "reference":
+        return reference_arm(spec, args, world, rank, chan)
+
+    import torch
+    import torch.distributed as dist
+    from selectssm_b200 import _lib
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev)
+    lib = _lib.load()
+    res = measure(spec, args, world, rank, dev, lib, chan=chan, bc_sum_mode=args.bc_sum)
+    line = {"metric": METRIC, "value": res["value"], "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": max(3, args.warmup), "ms_per_step": res["ms_per_step"], "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": res["dtype"], "data": "synthetic",
+            "config": config_of(spec, world, chan, res),
+            "roofline": res["roofline"], "roofline_fwd": res["roofline_fwd"], "roofline_step": res["roofline_step"],
+            "e2e": res["e2e"], "gpu_launches": res["gpu_launches"], "clocks": res["clocks"],
+            "library": lib.ssm_version().decode()}
+    if world == 1 and args.workload != 2 and not args.no_config2:
+        c2 = measure(SPECS[2], args, 1, 0, dev, lib, e2e=True)
+        line["config2"] = {"value": c2["value"], "unit": UNIT, "ms_per_step": c2["ms_per_step"],
+                           "dtype": "f32", "config": config_of(SPECS[2], 1, False, c2),
+                           "roofline": c2["roofline"], "roofline_fwd": c2["roofline_fwd"],
+                           "roofline_step": c2["roofline_step"], "e2e": c2["e2e"],
+                           "gpu_launches": c2["gpu_launches"], "clocks": c2["clocks"]}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        v, secs, sample = run_cpu_sample(batch=2)  # about 1 s on 16 cores: ~16 core-seconds of work
+        v, secs, sample = run_cpu_sample(spec, seqlen=spec["seqlen"], batch=4)  # about 1 s on 16 cores
         line["cpu_baseline"] = {"value": v, "unit": UNIT, "cores": cpu_cores(), "kind": "port",
                                 "sample": sample, "seconds": secs}
     if rank == 0:
         print(json.dumps(line))
     if world > 1:
         dist.destroy_process_group()
+
+
+def reference_arm(spec, args, world, rank, chan):
+    """The reference algorithm (NumPy restatement, oracle/) on the host cores,
+    on rank 0 only; each step is a bounded sample of the workload."""
+    if rank != 0:
+        return
+    steps = max(1, args.steps)
+    vals = []
+    # each step times the oracle on one full-width batch row of L=256, split
+    # over all host cores (about 0.1 s), so the run stays within minutes
+    sampler = CpuSampler(spec, 256)
+    for _ in range(args.warmup):
+        sampler.run()
+    t0 = time.perf_counter()
+    sample = ""
+    for _ in range(steps):
+        v, _, sample = sampler.run()
+        vals.append(v)
+    sampler.close()
+    total = time.perf_counter() - t0
+    v = statistics.median(vals)
+    cfg = {"workload": spec["workload"], "global_batch": spec["batch"], "seq_len": spec["seqlen"],
+           "d_inner": spec["dim"], "d_state": CFG["dstate"],
+           "parallelism": "host CPU (rank 0 only)" if world > 1 else "host CPU"}
+    line = {"metric": METRIC, "value": v, "unit": UNIT, "n_gpus": world, "steps": steps,
+            "warmup": args.warmup, "ms_per_step": 1e3 * total / steps, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": cfg,
+            "impl": "reference",
+            "cpu_baseline": {"value": v, "unit": UNIT, "cores": cpu_cores(), "kind": "port", "sample": sample},
+            "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line))
 
 
 if __name__ == "__main__":
