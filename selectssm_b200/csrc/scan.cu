@@ -228,17 +228,15 @@ static int check_bwd(const ssm_params_t* p, Geo* g) {
 static size_t round256(size_t x) { return (x + 255) & ~size_t(255); }
 
 // Sequence segments.  A (batch row, channel tile) is one chain of steps; with
-// few chains the sequence is cut into segments that run as separate CTAs, at
-// the price of a pre-pass over all segments but the last (it produces each
-// segment's end state / carry) and a fold.  The segment count minimises a
-// model of the run time in units of "one CTA processing one 16-step stage":
-//   waves(main) x stages per segment + r x waves(pre-pass) x stages per segment
-//   + a small per-segment cost,
-// where waves = ceil(CTAs / resident CTAs on the GPU).  Whole waves matter
-// because every CTA of a wave runs at about the same speed, so a last wave
-// that is a quarter full costs as much as a full one.  The resident counts are
-// the kernels' occupancy on a 148-SM B200 and are fixed here (not queried), so
-// workspace sizes stay a function of the shapes alone.
+// few chains the sequence is cut into segments that run as separate CTAs of
+// one launch: a segment that a later one depends on first runs an aggregate
+// pass over its own steps and publishes it, and every segment folds the
+// published values before it (decoupled lookback).  The segment count
+// minimises a model of the run time in units of "one CTA processing one
+// 16-step stage": the total work (main passes, aggregate passes at relative
+// cost r, a fixed cost per CTA) spread over the resident CTAs, plus the
+// duration of one CTA (the tail).  The resident counts are fixed here (not
+// queried), so workspace sizes stay a function of the shapes alone.
 struct Seg {
   int nseg, seg_chunks;
 };
@@ -253,17 +251,15 @@ struct SegPolicy {
   double cta_cost;  // fixed cost of one CTA in stages (set-up, pipeline fill, lookback)
 };
 constexpr int kSMs = 148;
-// The forward's CTAs are small and latency bound, so its "waves" are effective
-// sizes fitted to measurements (batch 8 runs best unsegmented with 384 CTAs,
-// batch 2 with 16 segments) rather than occupancy limits.
-// Its cap is lower because each segment folds the end states of all segments
-// before it (quadratic in the segment count).  Its fitted sizes hold per
-// direction: a bidirectional launch (B=2, L=131072, 512 channels) ran faster with the
+// The forward's CTAs are small and latency bound, so its resident-CTA count is
+// an effective size fitted to measurements (batch 8 runs best unsegmented with
+// 384 CTAs) rather than an occupancy limit.  Its choice holds per direction: a
+// bidirectional launch (B=2, L=131072, 512 channels) ran faster with the
 // per-direction choice than with one that counts both directions' chains.
 #ifndef SSM_FWD_SLOTS
 #define SSM_FWD_SLOTS 384
 #endif
-constexpr SegPolicy kFwdSeg{64, false, kTileCh, SSM_FWD_SLOTS, 4 * SSM_FWD_SLOTS, 0.55, false, 0.0};
+constexpr SegPolicy kFwdSeg{256, false, kTileCh, SSM_FWD_SLOTS, SSM_FWD_SLOTS, 0.8, true, 8.0};
 // The backward runs its aggregate passes inside the main launch, so CTAs of
 // all segments share the GPU: the model is the total work spread over the
 // resident CTAs plus the duration of the last CTA (the tail), with a fixed
@@ -317,11 +313,18 @@ static size_t wide_bc_bytes(const Geo& g) {
   return g.bcbf16 ? 2 * round256((size_t)g.B * g.L * kN * 4) : 0;
 }
 
+// lookback flags of one direction: a 16-byte word (the launch's CTA ticket,
+// used in the first direction's region) then one int per (row, tile, segment)
+static size_t flag_bytes(const Geo& g, int nseg, int tile) {
+  return round256(16 + (size_t)g.B * ((g.Dm + tile - 1) / tile) * nseg * 4);
+}
+
+// segI, flags
 static size_t fwd_seg_bytes(const Geo& g) {
   const Seg sg = choose_segments(g, kFwdSeg);
   if (sg.nseg <= 1) return 0;
   const size_t rows = (size_t)g.B * sg.nseg * g.Dm;
-  return round256(rows * kN * 4) + round256(rows * 4);
+  return round256(rows * kN * 4) + flag_bytes(g, sg.nseg, kTileCh);
 }
 
 static size_t fwd_ws_bytes(const Geo& g) { return fwd_seg_bytes(g) + wide_bc_bytes(g); }
@@ -331,18 +334,14 @@ static size_t bc_part_bytes(const Geo& g) {
   return round256((size_t)((g.Dm + kBTile - 1) / kBTile) * g.B * g.L * 2 * kN * 4);
 }
 
-// lookback flags of one direction: a 16-byte word (the launch's CTA ticket,
-// used in the first direction's region) then one int per (row, tile, segment)
-static size_t bwd_flag_bytes(const Geo& g, int nseg) {
-  return round256(16 + (size_t)g.B * ((g.Dm + kBTile - 1) / kBTile) * nseg * 4);
-}
+static size_t bwd_flag_bytes(const Geo& g, int nseg) { return flag_bytes(g, nseg, kBTile); }
 
 static size_t bwd_ws_bytes(const Geo& g, bool multicast = false) {
   const Seg sg = choose_segments(g, kBwdSeg);
   const size_t rows = (size_t)g.B * sg.nseg * g.Dm;
   size_t n = round256(rows * kN * 4) + 2 * round256(rows * 4);
-  if (sg.nseg > 1)  // segF, segT, segI, flags
-    n += 2 * round256(rows * kN * 4) + round256(rows * 4) + bwd_flag_bytes(g, sg.nseg);
+  if (sg.nseg > 1)  // segI, flags
+    n += round256(rows * kN * 4) + bwd_flag_bytes(g, sg.nseg);
   if (!multicast) n += bc_part_bytes(g);  // the multicast form sums dB / dC in the caller's buffer
   return n + wide_bc_bytes(g);
 }
@@ -420,8 +419,13 @@ static int fill_fwd_dir(const ssm_params_t* p, const Geo& g, FwdDir* d, cudaStre
   d->seg_chunks = sg.seg_chunks;
   if (sg.nseg > 1) {
     char* ws = static_cast<char*>(p->workspace);
-    d->segH = reinterpret_cast<float*>(ws);
-    d->segT = reinterpret_cast<float*>(ws + round256((size_t)g.B * sg.nseg * g.Dm * kN * 4));
+    const size_t rows = (size_t)g.B * sg.nseg * g.Dm;
+    d->segI = reinterpret_cast<float*>(ws);
+    ws += round256(rows * kN * 4);
+    int* flags = reinterpret_cast<int*>(ws);
+    d->seg_flag = flags + 4;  // after the ticket word
+    // lookback flags (and the ticket) start at zero on every call
+    SSM_CUDA_CHECK(cudaMemsetAsync(flags, 0, flag_bytes(g, sg.nseg, kTileCh), s), "cudaMemsetAsync(lookback flags)");
   }
   return SSM_OK;
 }
@@ -431,20 +435,16 @@ static int launch_fwd_t(FwdLaunch& L, int ndir, const Geo& g, cudaStream_t s) {
   constexpr int kBytes = FwdSmem<T, TBC>::kBytes;
   const int nseg = L.dir[0].nseg;
   dim3 grid((g.Dm + kTileCh - 1) / kTileCh, g.B, 1);
-  if (nseg > 1) {  // segment pre-pass: end state of every segment but the last
-    auto agg = ssm_fwd_kernel<T, TBC, true>;
-    SSM_CUDA_CHECK(cudaFuncSetAttribute(agg, cudaFuncAttributeMaxDynamicSharedMemorySize, kBytes),
-                   "cudaFuncSetAttribute(ssm_fwd_kernel<agg>)");
-    L.zdiv = nseg - 1;
-    grid.z = ndir * (nseg - 1);
-    agg<<<grid, kFThreads, kBytes, s>>>(L);
-    note_launches(1);
-  SSM_CUDA_CHECK(cudaGetLastError(), "launch ssm_fwd_kernel<agg>");
-  }
   L.zdiv = nseg;
   grid.z = ndir * nseg;
+  L.ntile = (int)grid.x;
+  L.batch = g.B;
+  L.chains = (int)grid.x * g.B * ndir;
+  L.ticket = nseg > 1 ? L.dir[0].seg_flag - 4 : nullptr;
+  L.spin_limit = kLookbackSpin;
   const bool wide = (long)grid.x * grid.y * grid.z <= (long)(kFMinBlocks / 2) * kSMs;
-  auto kern = wide ? ssm_fwd_kernel<T, TBC, false, true> : ssm_fwd_kernel<T, TBC, false, false>;
+  auto kern = nseg > 1 ? (wide ? ssm_fwd_kernel<T, TBC, true, true> : ssm_fwd_kernel<T, TBC, false, true>)
+                       : (wide ? ssm_fwd_kernel<T, TBC, true, false> : ssm_fwd_kernel<T, TBC, false, false>);
   SSM_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kBytes),
                  "cudaFuncSetAttribute(ssm_fwd_kernel)");
   kern<<<grid, kFThreads, kBytes, s>>>(L);
@@ -461,7 +461,7 @@ static int launch_fwd(FwdLaunch& L, int ndir, const Geo& g, cudaStream_t s) {
 
 // ---------------------------------------------------------------- backward launch
 struct BwdWs {
-  float *dA_part, *dD_part, *db_part, *bc_part, *dB_acc, *dC_acc, *segF, *segT, *segI, *Bw, *Cw;
+  float *dA_part, *dD_part, *db_part, *bc_part, *dB_acc, *dC_acc, *segI, *Bw, *Cw;
   int* flags;  // ticket word, then the lookback flags (null without segments)
   size_t flag_bytes;
   int64_t acc_stride;
@@ -476,14 +476,10 @@ static void carve_ws(const ssm_params_t* p, const Geo& g, char* ws, BwdWs* w, fl
   ws += round256(rows * 4);
   w->db_part = reinterpret_cast<float*>(ws);
   ws += round256(rows * 4);
-  w->segF = w->segT = w->segI = nullptr;
+  w->segI = nullptr;
   w->flags = nullptr;
   w->flag_bytes = 0;
   if (sg.nseg > 1) {
-    w->segF = reinterpret_cast<float*>(ws);
-    ws += round256(rows * kN * 4);
-    w->segT = reinterpret_cast<float*>(ws);
-    ws += round256(rows * 4);
     w->segI = reinterpret_cast<float*>(ws);
     ws += round256(rows * kN * 4);
     w->flags = reinterpret_cast<int*>(ws);
@@ -551,8 +547,6 @@ static int fill_bwd_dir(const ssm_params_t* p, const Geo& g, const BwdWs& w, Bwd
   const Seg sg = choose_segments(g, kBwdSeg);
   d->nseg = sg.nseg;
   d->seg_chunks = sg.seg_chunks;
-  d->segF = w.segF;
-  d->segT = w.segT;
   d->segI = w.segI;
   d->seg_flag = w.flags ? w.flags + 4 : nullptr;
   return SSM_OK;

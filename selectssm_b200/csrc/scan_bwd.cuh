@@ -349,80 +349,50 @@ __global__ void __launch_bounds__(kBThreads, 2) ssm_bwd_kernel(const __grid_cons
     }
   }
   int* wait_slot = reinterpret_cast<int*>(smem + S.offTmem + 8);
-  const size_t seg_row = (size_t)b * a.nseg + seg;
-  int* my_flag = a.seg_flag + ((size_t)b * P.ntile + tile) * a.nseg + seg;
-  if (lookback && !failed) {
+  if (lookback) {
+    // The adjoint entering this segment (at its last step) is the inclusive
+    // carry of the segment after it; each segment publishes its own as
+    // F + exp(A T) * that carry as soon as it knows it.  The aggregate passes
+    // of all segments run in parallel and only this short step is chained,
+    // always in segment order, so the result does not depend on timing.
+    failed = __syncthreads_or(failed);
     tsum += __shfl_xor_sync(kFull, tsum, 16);  // both halves' steps
-    const bool last = seg == a.nseg - 1;
-    if (nagg) {  // publish the aggregate (the last segment's is already inclusive)
-      float* dst = (last ? a.segI : a.segF) + (seg_row * Dm + c) * kN;
+    int* my_flag = a.seg_flag + ((size_t)b * P.ntile + tile) * a.nseg + seg;
+    float2 carry[4];
+#pragma unroll
+    for (int p = 0; p < 4; ++p) carry[p] = make_float2(0.f, 0.f);
+    if (!failed && seg < a.nseg - 1) {
+      if (cta_wait_flag(my_flag + 1, P.spin_limit, wait_slot) == 0) {
+        failed = true;
+      } else {
+        const float* src = a.segI + (((size_t)b * a.nseg + seg + 1) * Dm + (cvalid ? c : 0)) * kN;
+        const float4 x0 = __ldcg(reinterpret_cast<const float4*>(src + q0));
+        const float4 x1 = __ldcg(reinterpret_cast<const float4*>(src + (q0 ^ 4)));
+        carry[0] = make_float2(x0.x, x0.y);
+        carry[1] = make_float2(x0.z, x0.w);
+        carry[2] = make_float2(x1.x, x1.y);
+        carry[3] = make_float2(x1.z, x1.w);
+      }
+    }
+    if (!failed && nagg) {  // publish the inclusive carry: F + exp(A T) carry
+      const float2 t2 = dup2(tsum);
+      float2 I[4];
+#pragma unroll
+      for (int p = 0; p < 4; ++p) {
+        const float2 e = fmul2(A2[p], t2);
+        I[p] = ffma2(make_float2(ex2(e.x), ex2(e.y)), carry[p], fa[p]);
+      }
       if (cvalid) {
-        *reinterpret_cast<float4*>(dst + q0) = make_float4(fa[0].x, fa[0].y, fa[1].x, fa[1].y);
-        *reinterpret_cast<float4*>(dst + (q0 ^ 4)) = make_float4(fa[2].x, fa[2].y, fa[3].x, fa[3].y);
-        if (hs == 0) a.segT[seg_row * Dm + c] = tsum;
+        float* dst = a.segI + (((size_t)b * a.nseg + seg) * Dm + c) * kN;
+        *reinterpret_cast<float4*>(dst + q0) = make_float4(I[0].x, I[0].y, I[1].x, I[1].y);
+        *reinterpret_cast<float4*>(dst + (q0 ^ 4)) = make_float4(I[2].x, I[2].y, I[3].x, I[3].y);
       }
       __threadfence();
       __syncthreads();
-      if (threadIdx.x == 0) st_release_gpu(my_flag, last ? kInclReady : kAggReady);
+      if (threadIdx.x == 0) st_release_gpu(my_flag, kInclReady);
     }
-    if (last) {  // nothing enters the last segment: its main pass starts from zero
 #pragma unroll
-      for (int p = 0; p < 4; ++p) fa[p] = make_float2(0.f, 0.f);
-    }
-    if (!last) {
-      // fold the published carries of the later segments: carry entering this
-      // segment = sum_s' exp(A * sum of dt of the segments between) * X_s',
-      // X the aggregate, or the inclusive carry (which ends the walk)
-      float2 carry[4];
-#pragma unroll
-      for (int p = 0; p < 4; ++p) carry[p] = make_float2(0.f, 0.f);
-      float tacc = 0.f;
-      for (int sp = seg + 1; sp < a.nseg; ++sp) {
-        const int f = cta_wait_flag(my_flag + (sp - seg), P.spin_limit, wait_slot);
-        if (f == 0) {
-          failed = true;
-          break;
-        }
-        const size_t row = ((size_t)b * a.nseg + sp) * Dm + (cvalid ? c : 0);
-        float2 X[4];
-        {
-          const float* src = (f == kInclReady ? a.segI : a.segF) + row * kN;
-          const float4 x0 = __ldcg(reinterpret_cast<const float4*>(src + q0));
-          const float4 x1 = __ldcg(reinterpret_cast<const float4*>(src + (q0 ^ 4)));
-          X[0] = make_float2(x0.x, x0.y);
-          X[1] = make_float2(x0.z, x0.w);
-          X[2] = make_float2(x1.x, x1.y);
-          X[3] = make_float2(x1.z, x1.w);
-        }
-        const float2 t2 = dup2(tacc);
-#pragma unroll
-        for (int p = 0; p < 4; ++p) {
-          const float2 e = fmul2(A2[p], t2);
-          carry[p] = ffma2(make_float2(ex2(e.x), ex2(e.y)), X[p], carry[p]);
-        }
-        if (f == kInclReady) break;
-        tacc += __ldcg(a.segT + row);
-      }
-      if (!failed && seg > 0) {  // publish the inclusive carry: F + exp(A T) carry
-        const float2 t2 = dup2(tsum);
-        float2 I[4];
-#pragma unroll
-        for (int p = 0; p < 4; ++p) {
-          const float2 e = fmul2(A2[p], t2);
-          I[p] = ffma2(make_float2(ex2(e.x), ex2(e.y)), carry[p], fa[p]);
-        }
-        if (cvalid) {
-          float* dst = a.segI + (seg_row * Dm + c) * kN;
-          *reinterpret_cast<float4*>(dst + q0) = make_float4(I[0].x, I[0].y, I[1].x, I[1].y);
-          *reinterpret_cast<float4*>(dst + (q0 ^ 4)) = make_float4(I[2].x, I[2].y, I[3].x, I[3].y);
-        }
-        __threadfence();
-        __syncthreads();
-        if (threadIdx.x == 0) st_release_gpu(my_flag, kInclReady);
-      }
-#pragma unroll
-      for (int p = 0; p < 4; ++p) fa[p] = carry[p];  // the main pass starts from the true carry
-    }
+    for (int p = 0; p < 4; ++p) fa[p] = carry[p];  // the main pass starts from the true carry
   }
 
   for (int it = 0; it < nloc && !failed; ++it) {

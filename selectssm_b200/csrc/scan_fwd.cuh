@@ -37,7 +37,10 @@ namespace ssm {
 
 
 constexpr int kFThreads = 4 * kTileCh;  // 4 lanes per channel, 8 channels per warp
-constexpr int kFMinBlocks = 768 / kFThreads;  // resident CTAs per SM at <= 80 registers
+#ifndef SSM_FWD_MINB
+#define SSM_FWD_MINB 6
+#endif
+constexpr int kFMinBlocks = SSM_FWD_MINB * 128 / kFThreads;  // resident CTAs per SM (80 registers at 6)
 constexpr int kFStages = 3;
 
 template <typename T, typename TBC>
@@ -48,22 +51,36 @@ struct FwdSmem {
   static constexpr int kOffB = 4 * kAct, kOffC = 4 * kAct + kBC;
   static constexpr int kStage = 4 * kAct + 2 * kBC;
   static constexpr int kBars = kStage * kFStages;  // full[kFStages] then empty[kFStages]
-  static constexpr int kBytes = kBars + 16 * kFStages;
+  static constexpr int kBytes = kBars + 16 * kFStages + 16;  // + ticket / flag broadcast words
 };
 
 
-// WIDE: the grid fills at most 3 CTAs per SM, so each thread may use up to 168
-// registers (more scheduling freedom); otherwise 6 CTAs per SM fit (80).
-template <typename T, typename TBC, bool AGG, bool WIDE = false>
+// WIDE: the grid fills at most half the resident CTAs, so each thread may use
+// up to twice the registers (more scheduling freedom).
+// SEG: the launch cuts the sequence into segments (lookback code compiled in).
+template <typename T, typename TBC, bool WIDE, bool SEG>
 __global__ void __launch_bounds__(kFThreads, WIDE ? kFMinBlocks / 2 : kFMinBlocks) ssm_fwd_kernel(const __grid_constant__ FwdLaunch P) {
   using S = FwdSmem<T, TBC>;
-  const FwdDir& a = P.dir[blockIdx.z / P.zdiv];
-  const int seg = blockIdx.z % P.zdiv;
   extern __shared__ __align__(1024) unsigned char smem[];
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::kBars);
+  int* bcast = reinterpret_cast<int*>(smem + S::kBars + 16 * kFStages);  // ticket, lookback flag
 
-  const int b = blockIdx.y;
-  const int c0 = blockIdx.x * kTileCh;
+  // CTA identity: with segments, from an atomic ticket in scan order (first
+  // segments first, so every segment a CTA waits for is already running);
+  // otherwise from the block index.  Grid: (channel tiles, batch, directions x segments).
+  int tile = blockIdx.x, b = blockIdx.y, dz = blockIdx.z;
+  if (SEG) {
+    if (threadIdx.x == 0) bcast[0] = atomicAdd(P.ticket, 1);
+    __syncthreads();
+    const int k = bcast[0];
+    const int r = k % P.chains;
+    tile = r % P.ntile;
+    b = (r / P.ntile) % P.batch;
+    dz = (r / (P.ntile * P.batch)) * P.zdiv + k / P.chains;
+  }
+  const FwdDir& a = P.dir[dz / P.zdiv];
+  const int seg = dz % P.zdiv;
+  const int c0 = tile * kTileCh;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nq = lane & 3;
   const int cl = warp * 8 + (lane >> 2);
@@ -84,6 +101,12 @@ __global__ void __launch_bounds__(kFThreads, WIDE ? kFMinBlocks / 2 : kFMinBlock
   const bool cvalid = c < Dm;
   const int co = comp ? Dm - 1 - c : c;
   const int oc0 = comp ? Dm - kTileCh - c0 : c0;
+  // Loads: first the aggregate pass over the segment (segments that a later
+  // CTA waits for; u, delta, B only), then the main pass; load g uses stage
+  // g % kFStages.
+  constexpr bool lookback = SEG;
+  const int nagg = (lookback && seg < a.nseg - 1) ? nloc : 0;
+  const int ntot = nagg + nloc;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kFStages; ++s) {
@@ -94,26 +117,27 @@ __global__ void __launch_bounds__(kFThreads, WIDE ? kFMinBlocks / 2 : kFMinBlock
   }
   __syncthreads();
 
-  const uint32_t tx = AGG ? 2 * S::kAct + S::kBC
-                          : 2 * S::kAct + 2 * S::kBC + (has_z ? S::kAct : 0) + (need_uo ? S::kAct : 0);
-  auto issue = [&](int jl) {
-    unsigned char* st = smem + (jl % kFStages) * S::kStage;
-    uint64_t* bar = &bars[jl % kFStages];
-    const int t0 = (j0 + jl) * kChunk;
+  const uint32_t tx_agg = 2 * S::kAct + S::kBC;
+  const uint32_t tx = 2 * S::kAct + 2 * S::kBC + (has_z ? S::kAct : 0) + (need_uo ? S::kAct : 0);
+  auto issue = [&](int g) {
+    const bool ag = g < nagg;
+    unsigned char* st = smem + (g % kFStages) * S::kStage;
+    uint64_t* bar = &bars[g % kFStages];
+    const int t0 = (j0 + (ag ? g : g - nagg)) * kChunk;
     const int ot0 = rev ? L - kChunk - t0 : t0;
-    mbar_arrive_expect_tx(bar, tx);
+    mbar_arrive_expect_tx(bar, ag ? tx_agg : tx);
     tma_load_3d(st + S::kOffU, &a.tm_u, bar, c0, t0, b);
     tma_load_3d(st + S::kOffDelta, &a.tm_delta, bar, c0, t0, b);
     tma_load_3d(st + S::kOffB, &a.tm_B, bar, 0, t0, b);
-    if (!AGG) {
+    if (!ag) {
       tma_load_3d(st + S::kOffC, &a.tm_C, bar, 0, t0, b);
       if (has_z) tma_load_3d(st + S::kOffZ, &a.tm_z, bar, oc0, ot0, b);
       if (need_uo) tma_load_3d(st + S::kOffUo, &a.tm_u, bar, oc0, ot0, b);
     }
   };
   if (threadIdx.x == 0) {
-    const int npre = nloc < kFStages ? nloc : kFStages;
-    for (int jl = 0; jl < npre; ++jl) issue(jl);
+    const int npre = ntot < kFStages ? ntot : kFStages;
+    for (int g = 0; g < npre; ++g) issue(g);
   }
 
   float2 A2[2];
@@ -126,28 +150,19 @@ __global__ void __launch_bounds__(kFThreads, WIDE ? kFMinBlocks / 2 : kFMinBlock
   const float bias = (a.bias && cvalid) ? a.bias[c] : 0.f;
   const float Dsk = (has_D && cvalid) ? a.D[aligned ? c : co] : 0.f;
   float2 h[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
-  if (!AGG && cvalid) {  // fold the end states of the preceding segments
-    for (int sp = 0; sp < seg; ++sp) {
-      const size_t r = (size_t)b * a.nseg + sp;
-      const float Tsum = a.segT[r * Dm + c];
-      const float4 H = *reinterpret_cast<const float4*>(a.segH + (r * Dm + c) * kN + 4 * nq);
-      const float2 e0 = fmul2(A2[0], dup2(Tsum)), e1 = fmul2(A2[1], dup2(Tsum));
-      h[0] = ffma2(make_float2(ex2(e0.x), ex2(e0.y)), h[0], make_float2(H.x, H.y));
-      h[1] = ffma2(make_float2(ex2(e1.x), ex2(e1.y)), h[1], make_float2(H.z, H.w));
-    }
-  }
   float tsum = 0.f;
   T* out = reinterpret_cast<T*>(a.out);
   const bool b1 = (nq & 2) != 0, b0 = (nq & 1) != 0;
+  bool failed = false;
 
-  for (int j = j0; j < j1; ++j) {
-    const int jl = j - j0;
-    const int s = jl % kFStages;
-    const bool ok = mbar_wait_bounded(&bars[s], (jl / kFStages) & 1);
-    if (!__all_sync(kFull, ok)) {  // warps proceed independently; a stalled load ends this warp
-      if (lane == 0) report(a.status, kStatusTimeout);
-      return;
-    }
+  // One 16-step stage (load g, chunk j).  AGG: the recurrence only (no y,
+  // checkpoints or outputs).  Returns false if a bounded wait gave up.
+  auto run_stage = [&](auto agg_c, int g) -> bool {
+    constexpr bool AGG = decltype(agg_c)::value;
+    const int j = j0 + (AGG ? g : g - nagg);
+    const int s = g % kFStages;
+    const bool ok = mbar_wait_bounded(&bars[s], (g / kFStages) & 1);
+    if (!__all_sync(kFull, ok)) return false;  // warps proceed independently
     const unsigned char* st = smem + s * S::kStage;
     const T* su = reinterpret_cast<const T*>(st + S::kOffU);
     const T* sd = reinterpret_cast<const T*>(st + S::kOffDelta);
@@ -165,7 +180,7 @@ __global__ void __launch_bounds__(kFThreads, WIDE ? kFMinBlocks / 2 : kFMinBlock
       dt = valid ? dt : 0.f;
       dtv[i] = dt;
       dxv[i] = valid ? dt * x : 0.f;
-      tsum += dt;
+      if (AGG) tsum += dt;
     }
 
     float yv[4];
@@ -236,24 +251,60 @@ __global__ void __launch_bounds__(kFThreads, WIDE ? kFMinBlocks / 2 : kFMinBlock
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&bars[kFStages + s]);  // this warp no longer reads stage s
-    if (threadIdx.x == 0 && jl + kFStages < nloc) {  // refill stage s once every warp released it
-      if (!mbar_wait_bounded(&bars[kFStages + s], (jl / kFStages) & 1)) {
-        report(a.status, kStatusTimeout);
-        return;
+    bool rok = true;
+    if (threadIdx.x == 0 && g + kFStages < ntot) {  // refill stage s once every warp released it
+      rok = mbar_wait_bounded(&bars[kFStages + s], (g / kFStages) & 1);
+      if (rok) {
+        fence_proxy_async_smem();
+        issue(g + kFStages);
       }
-      fence_proxy_async_smem();
-      issue(jl + kFStages);
     }
-  }
-  if (AGG) {
+    return __shfl_sync(kFull, rok, 0);  // warp-uniform (lane 0 of warp 0 refills)
+  };
+
+  // ---- aggregate pass: this segment's end state from a zero start and its
+  // sum of dt, folded by the segments after it (the chunk carry of
+  // src/selectssm/selectssm.py:87, 91 and 107).
+  for (int g = 0; g < nagg && !failed; ++g) failed = !run_stage(std::true_type{}, g);
+  if (lookback) {
+    // The state entering this segment is the inclusive end state of the one
+    // before it; each segment publishes its own as H + exp(A T) * that state as
+    // soon as it knows it.  The aggregate passes of all segments run in
+    // parallel and only this short step is chained, always in segment order,
+    // so the result does not depend on timing.
+    failed = __syncthreads_or(failed);
     tsum += __shfl_xor_sync(kFull, tsum, 1);
     tsum += __shfl_xor_sync(kFull, tsum, 2);
-    if (cvalid) {
-      const size_t r = (size_t)b * a.nseg + seg;
-      *reinterpret_cast<float4*>(a.segH + (r * Dm + c) * kN + 4 * nq) = make_float4(h[0].x, h[0].y, h[1].x, h[1].y);
-      if (nq == 0) a.segT[r * Dm + c] = tsum;
+    int* my_flag = a.seg_flag + ((size_t)b * P.ntile + tile) * a.nseg + seg;
+    float2 carry[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+    if (!failed && seg > 0) {
+      if (cta_wait_flag(my_flag - 1, P.spin_limit, bcast + 1) == 0) {
+        failed = true;
+      } else {
+        const size_t row = ((size_t)b * a.nseg + seg - 1) * Dm + (cvalid ? c : 0);
+        const float4 X = __ldcg(reinterpret_cast<const float4*>(a.segI + row * kN + 4 * nq));
+        carry[0] = make_float2(X.x, X.y);
+        carry[1] = make_float2(X.z, X.w);
+      }
     }
+    if (!failed && nagg) {  // publish the inclusive end state: H + exp(A T) carry
+      const float2 t2 = dup2(tsum);
+      const float2 e0 = fmul2(A2[0], t2), e1 = fmul2(A2[1], t2);
+      const float2 i0 = ffma2(make_float2(ex2(e0.x), ex2(e0.y)), carry[0], h[0]);
+      const float2 i1 = ffma2(make_float2(ex2(e1.x), ex2(e1.y)), carry[1], h[1]);
+      if (cvalid)
+        *reinterpret_cast<float4*>(a.segI + (((size_t)b * a.nseg + seg) * Dm + c) * kN + 4 * nq) =
+            make_float4(i0.x, i0.y, i1.x, i1.y);
+      __threadfence();
+      __syncthreads();
+      if (threadIdx.x == 0) st_release_gpu(my_flag, kInclReady);
+    }
+    h[0] = carry[0];  // the main pass starts from the true state entering the segment
+    h[1] = carry[1];
   }
+  // ---- main pass
+  for (int g = nagg; g < ntot && !failed; ++g) failed = !run_stage(std::false_type{}, g);
+  if (failed && lane == 0) report(a.status, kStatusTimeout);
 }
 
 }  // namespace ssm

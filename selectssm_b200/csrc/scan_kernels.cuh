@@ -3,11 +3,8 @@
 // lookback helpers.
 //
 // Segments: when there are too few (batch row, channel tile) chains to fill
-// the GPU the sequence is cut into segments that run as separate CTAs.  The
-// forward's pre-pass computes each segment's end state from a zero start plus
-// its sum of dt and the main pass folds those of the preceding segments into
-// its start state; the backward does the same for the adjoint inside one
-// launch, with flags (decoupled lookback).
+// the GPU the sequence is cut into segments that run as separate CTAs of the
+// same launch, joined by flagged carries (see "segment carries").
 #pragma once
 
 #include "common.cuh"
@@ -26,8 +23,8 @@ struct FwdDir {
   void* out;
   float* states;
   int32_t* status;
-  float* segH;    // (B, nseg, D, 16) segment end states from a zero start
-  float* segT;    // (B, nseg, D) sum of dt over each segment
+  float* segI;    // (B, nseg, D, 16) inclusive end state of each segment
+  int* seg_flag;  // (B, channel tiles, nseg) lookback flags
   int64_t out_stride;
   int L, Dm, flags, gate_act, has_z;
   int nseg, seg_chunks;  // sequence segments (each seg_chunks chunks of 16 steps)
@@ -35,6 +32,9 @@ struct FwdDir {
 struct FwdLaunch {
   FwdDir dir[2];
   int zdiv;  // blockIdx.z = direction * zdiv + segment
+  int* ticket;  // CTA order counter (zeroed per call); null when nothing is segmented
+  int chains, ntile, batch;
+  uint32_t spin_limit;
 };
 
 struct BwdDir {
@@ -53,10 +53,8 @@ struct BwdDir {
   float* dA_part;  // (B, nseg, D, 16)
   float* dD_part;  // (B, nseg, D)
   float* db_part;  // (B, nseg, D)
-  float* segF;     // (B, nseg, D, 16) adjoint carried out of each segment's first step, zero start
-  float* segT;     // (B, nseg, D) sum of dt over each segment
-  float* segI;     // (B, nseg, D, 16) adjoint carried out of each segment's first step, true start
-  int* seg_flag;   // (B, channel tiles, nseg) lookback flags: kAggReady / kInclReady
+  float* segI;     // (B, nseg, D, 16) adjoint carried out of each segment's first step
+  int* seg_flag;   // (B, channel tiles, nseg) flags: the segment's segI is published
   int32_t* status;
   int64_t z_stride, acc_stride;
   int L, Dm, flags, gate_act, has_z;
@@ -76,15 +74,14 @@ struct BwdLaunch {
   uint32_t spin_limit;  // polls of a lookback flag before giving up
 };
 
-// ---------------------------------------------------------------- decoupled lookback
-// Segments of one chain publish, per channel, their zero-start aggregate
-// (flag kAggReady) and later their inclusive carry (flag kInclReady); a CTA
-// folds the published values of the segments before it (in scan order) until
-// it meets an inclusive one.  CTAs take their segment from an atomic ticket in
-// scan order, so every segment a CTA waits for belongs to a CTA that is
-// already resident or finished.
-constexpr int kAggReady = 1;
-constexpr int kInclReady = 2;
+// ---------------------------------------------------------------- segment carries
+// Segments of one chain run their aggregate passes (the recurrence over their
+// own steps from a zero start) in parallel; each then waits for the inclusive
+// carry of its neighbour in scan order (flag kInclReady), composes its own and
+// publishes it.  CTAs take their segment from an atomic ticket in scan order,
+// so every segment a CTA waits for belongs to a CTA that is already resident
+// or finished.
+constexpr int kInclReady = 1;
 constexpr uint32_t kLookbackSpin = 1u << 22;  // polls (each sleeps ~0.1 us): seconds, far above any real wait
 
 __device__ __forceinline__ int ld_acquire_gpu(const int* p) {
