@@ -233,9 +233,10 @@ static size_t round256(size_t x) { return (x + 255) & ~size_t(255); }
 // pass over its own steps and publishes it, and every segment folds the
 // published values before it (decoupled lookback).  The segment count
 // minimises a model of the run time in units of "one CTA processing one
-// 16-step stage": the total work (main passes, aggregate passes at relative
-// cost r, a fixed cost per CTA) spread over the resident CTAs, plus the
-// duration of one CTA (the tail).  The resident counts are fixed here (not
+// 16-step stage", from the duration of one CTA (its main pass, its aggregate
+// pass at relative cost r, a fixed cost) and the number of resident CTAs:
+// the total work spread evenly plus one CTA's duration (the tail).  The
+// backward instead follows a fill rule fitted to measurements.  The resident counts are fixed here (not
 // queried), so workspace sizes stay a function of the shapes alone.
 struct Seg {
   int nseg, seg_chunks;
@@ -249,6 +250,7 @@ struct SegPolicy {
   double agg_cost;  // pre-pass cost of one stage relative to the main kernel's
   bool single_pass; // pre-pass inside the main launch (decoupled lookback)
   double cta_cost;  // fixed cost of one CTA in stages (set-up, pipeline fill, lookback)
+  bool fill_rule;   // pick by the fill rule below instead of the cost model
 };
 constexpr int kSMs = 148;
 // The forward's CTAs are small and latency bound, so its resident-CTA count is
@@ -259,12 +261,8 @@ constexpr int kSMs = 148;
 #ifndef SSM_FWD_SLOTS
 #define SSM_FWD_SLOTS 384
 #endif
-constexpr SegPolicy kFwdSeg{256, false, kTileCh, SSM_FWD_SLOTS, SSM_FWD_SLOTS, 0.8, true, 8.0};
-// The backward runs its aggregate passes inside the main launch, so CTAs of
-// all segments share the GPU: the model is the total work spread over the
-// resident CTAs plus the duration of the last CTA (the tail), with a fixed
-// cost per CTA.
-constexpr SegPolicy kBwdSeg{256, true, kBTile, 2L * kSMs, 2L * kSMs, 0.35, true, 8.0};
+constexpr SegPolicy kFwdSeg{256, false, kTileCh, SSM_FWD_SLOTS, SSM_FWD_SLOTS, 0.8, true, 8.0, false};
+constexpr SegPolicy kBwdSeg{256, true, kBTile, 2L * kSMs, 2L * kSMs, 0.2, true, 2.0, true};  // fill rule
 
 static Seg choose_segments(const Geo& g, SegPolicy pol) {
   const int nblk = (g.L + kChunk - 1) / kChunk;
@@ -284,6 +282,20 @@ static Seg choose_segments(const Geo& g, SegPolicy pol) {
   int max_seg = nblk / 4;  // at least 4 stages (64 steps) per segment
   if (max_seg < 1) max_seg = 1;
   if (max_seg > pol.max_seg) max_seg = pol.max_seg;
+  if (pol.fill_rule) {
+    // Measured on the backward (batches 8 to 64 of 1536 channels): with at
+    // least two waves of chains the sequence is not cut; otherwise as many
+    // segments as fit in two waves of CTAs (four when that is fewer than two
+    // segments), and at least one per 64 stages (1024 steps), since shorter
+    // CTAs balance better across the SMs than a few long ones.
+    if (chains >= 2 * pol.slots) return {1, nblk};
+    long n = 2 * pol.slots / chains;
+    if (n < 2) n = 4 * pol.slots / chains;
+    n = std::max<long>(n, nblk / 64);
+    if (n > max_seg) n = max_seg;
+    const int sc = (nblk + (int)n - 1) / (int)n;
+    return {(nblk + sc - 1) / sc, sc};
+  }
   double best = 0.0;
   Seg pick{1, nblk};
   for (int n = 1; n <= max_seg; ++n) {
@@ -291,7 +303,7 @@ static Seg choose_segments(const Geo& g, SegPolicy pol) {
     const int nseg = (nblk + seg_chunks - 1) / seg_chunks;
     if (nseg != n) continue;  // the same split as a smaller n
     double cost;
-    if (pol.single_pass) {
+    if (pol.single_pass) {  // CTAs that each run an aggregate pass and a main pass
       const double per_cta = seg_chunks * (1.0 + (nseg > 1 ? pol.agg_cost : 0.0)) + pol.cta_cost;
       const double work = (double)chains * (seg_chunks * (nseg + pol.agg_cost * (nseg - 1)) + pol.cta_cost * nseg);
       cost = work / pol.slots + per_cta;
