@@ -172,6 +172,26 @@ class SelectiveSSM(nn.Module):
             self.sown["ssm_output_mean"], self.sown["ssm_output_sd"] = y.mean(), y.std()
         return y
 
+    def forward_rc(self, x, train: bool = False):
+        """rc(self(rc(x))) with rc(x)[b, l, d] = x[b, L-1-l, D-1-d]: the antisense
+        strand of an RCPS wrapper (rcps.py:42-72), computed without flipping
+        anything in memory.  The reversed, complemented read of the conv and
+        scan kernels takes the place of the input flip, their unflipped store
+        takes the place of the output flip, and the skip stays in the scan
+        frame.  Only for a forward (reverse=False, complement=False) module."""
+        if self.reverse or self.complement:
+            raise ValueError("forward_rc needs a module with reverse=False and complement=False")
+        self.reverse, self.complement = True, True
+        try:
+            u, delta, A, Bm, Cm, bias = self.scan_inputs(x)
+        finally:
+            self.reverse, self.complement = False, False
+        y = ops.selective_scan(u, delta, A, Bm, Cm, D=self.D, delta_bias=bias, delta_softplus=True,
+                               reverse=True, complement=True, aligned_skip=True)
+        if self.regularize:
+            self.sown["ssm_regularizer"] = self.regularizer()
+        return y
+
     # ---- Flax parameter trees
     def load_flax_params(self, tree):
         """Copy a Flax SelectiveSSM parameter dict (numpy or torch arrays)."""

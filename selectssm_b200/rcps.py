@@ -6,10 +6,12 @@ carries the sense strand in channels [0, D) and the antisense strand in
 [D, 2D); shared weights process both.
 
 Difference from the reference, with the same result: RCPSWrapper
-(rcps.py:42-72) calls its inner module twice, once per strand.  Here the sense
-strand and the conjugated antisense strand are stacked along the batch axis
-and the inner module runs once on 2B rows, so its kernels launch once per layer
-with twice the work.  This relies on the inner module treating batch rows
+(rcps.py:42-72) calls its inner module twice, once per strand, on a flipped
+copy of the antisense strand.  Here a forward SelectiveSSM inner module runs
+the antisense strand through its reversed, complemented in-place read
+(SelectiveSSM.forward_rc), so no flipped copy is made; any other inner module
+gets the sense strand and the conjugated antisense strand stacked along the
+batch axis and runs once on 2B rows.  This relies on the inner module treating batch rows
 independently, which SelectiveSSM, BidirectionalMamba and every norm here do.
 """
 
@@ -47,6 +49,11 @@ class RCPSWrapper(nn.Module):
     def forward(self, x: torch.Tensor, **kwargs) -> torch.Tensor:
         D = x.shape[-1] // 2
         sense, antisense = x[..., :D], x[..., D:]
+        rc_inner = getattr(self.inner, "forward_rc", None)
+        if rc_inner is not None and not (self.inner.reverse or self.inner.complement):
+            # a forward SelectiveSSM reads the antisense strand reversed and
+            # complemented in place (no flipped copies in or out)
+            return torch.cat([self.inner(sense, **kwargs), rc_inner(antisense, **kwargs)], dim=-1)
         both = torch.cat([sense, rc_conjugate(antisense)], dim=0)  # (2B, L, D): one inner call
         out = self.inner(both, **kwargs)
         B = x.shape[0]

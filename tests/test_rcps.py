@@ -71,3 +71,31 @@ def test_wrapper_around_bidirectional_mamba(cuda):
     assert ((rc_conjugate(y) - model(rc_conjugate(x))).abs().max() / scale) < 1e-4
     (y ** 2).sum().backward()
     assert all(p.grad is not None and torch.isfinite(p.grad).all() for p in inner.parameters())
+
+
+@pytest.mark.gpu
+def test_wrapper_around_selective_ssm_reads_antisense_in_place(cuda, monkeypatch):
+    """A forward SelectiveSSM inner module runs the antisense strand through the
+    kernels' reversed, complemented read: no flipped copy is made, and the
+    result equals the reference's rc(inner(rc(x))) (rcps.py:42-72)."""
+    import selectssm_b200.rcps as R
+    from selectssm_b200 import SelectiveSSM
+    torch.manual_seed(5)
+    inner = SelectiveSSM(48, hidden_features=16, shift_conv_size=4).to(cuda)
+    with torch.no_grad():
+        inner.D.uniform_(0.5, 1.5)  # a non-trivial skip, so its frame matters
+    model = RCPSWrapper(inner)
+    x = torch.randn(2, 200, 96, device=cuda)
+    ref = torch.cat([inner(x[..., :48]), rc_conjugate(inner(rc_conjugate(x[..., 48:])))], dim=-1)
+
+    def no_flip(t):
+        raise AssertionError("the antisense strand was flipped in memory")
+
+    monkeypatch.setattr(R, "rc_conjugate", no_flip)
+    y = model(x)
+    monkeypatch.undo()
+    scale = ref.abs().max()
+    assert ((y - ref).abs().max() / scale) < 1e-5
+    assert ((rc_conjugate(y) - model(rc_conjugate(x))).abs().max() / scale) < 1e-4
+    (y ** 2).sum().backward()
+    assert all(p.grad is not None and torch.isfinite(p.grad).all() for p in inner.parameters())
