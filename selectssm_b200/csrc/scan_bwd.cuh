@@ -36,14 +36,14 @@
 //   per-step work holds no data- or flag-dependent branch (only stores are
 //   predicated), so the compiler can schedule across the unrolled steps.
 // Segments: with few (batch row, channel tile) chains the sequence is cut into
-//   segments run by separate CTAs in one launch (single-pass decoupled
-//   lookback).  A CTA takes its segment from an atomic ticket, last segment
-//   first; for a segment that an earlier one waits on it first runs the
-//   adjoint over its own steps from a zero carry (the aggregate pass: delta, C,
-//   dout, z only) and publishes that carry and its sum of dt under a flag; it
-//   then folds the published values of the later segments (bounded waits) into
-//   the carry entering its own last step, publishes its inclusive carry, and
-//   runs the main pass from it.
+//   segments run by separate CTAs of one launch.  A CTA takes its segment from
+//   an atomic ticket, last segment first.  A segment that an earlier one
+//   depends on first runs the adjoint over its own steps from a zero carry
+//   (the aggregate pass: delta, C, dout, z only), keeping that carry and its
+//   sum of dt in registers; it then waits (bounded) for the inclusive carry of
+//   the segment after it, publishes its own (F + exp(A T) carry) under a flag
+//   and runs the main pass from the true carry.  Only that short step is
+//   chained, in segment order, so the result does not depend on timing.
 #pragma once
 
 #include "scan_kernels.cuh"

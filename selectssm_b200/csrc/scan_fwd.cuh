@@ -22,10 +22,13 @@
 // complement unflip (:230-231) and the gate y * act(z) (:335-338).  The state
 // after every 8 steps is written to `states` for the backward.
 //
-// AGG: the segment pre-pass.  It runs one segment from a zero state and writes
-// only the segment's end state and its sum of dt; the main pass starts segment
-// s from the end states of segments 0..s-1 folded together
-// (h <- exp(A sum dt) h + H).
+// Segments (SEG launches): a CTA takes its segment from an atomic ticket in
+// scan order; a segment that a later one depends on first runs the recurrence
+// over its own steps from a zero state (the aggregate pass: u, delta, B only),
+// keeping the end state H and its sum of dt T in registers, then waits
+// (bounded) for the inclusive end state of the segment before it, publishes
+// its own (H + exp(A T) carry) under a flag and runs the main pass from the
+// true state.  Only that short step is chained, in segment order.
 #pragma once
 
 #include <type_traits>
