@@ -583,7 +583,11 @@ static int launch_bwd_t(BwdLaunch& L, int ndir, const Geo& g, cudaStream_t s, co
   }
   const int nseg = L.dir[0].nseg;
   dim3 grid((g.Dm + kBTile - 1) / kBTile, g.B, 1);
-  auto kern = L.dir[0].bc_mode == kBcMulticast ? ssm_bwd_kernel<T, TBC, G, true> : ssm_bwd_kernel<T, TBC, G, false>;
+  const BwdDir& d0 = L.dir[0];
+  const bool fast = ndir == 1 && !(d0.flags & SSM_REVERSE) && (d0.flags & SSM_DELTA_SOFTPLUS);
+  const bool mc = d0.bc_mode == kBcMulticast;
+  auto kern = mc ? (fast ? ssm_bwd_kernel<T, TBC, G, true, true> : ssm_bwd_kernel<T, TBC, G, true, false>)
+                 : (fast ? ssm_bwd_kernel<T, TBC, G, false, true> : ssm_bwd_kernel<T, TBC, G, false, false>);
   SSM_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes),
                  "cudaFuncSetAttribute(ssm_bwd_kernel)");
   L.zdiv = nseg;
@@ -606,6 +610,7 @@ static int launch_bwd_t(BwdLaunch& L, int ndir, const Geo& g, cudaStream_t s, co
 
 template <typename T, typename TBC>
 static int launch_bwd_g(BwdLaunch& L, int ndir, const Geo& g, cudaStream_t s, const BwdHook* hook) {
+  if (!L.dir[0].has_z) return launch_bwd_t<T, TBC, -1>(L, ndir, g, s, hook);
   switch (L.dir[0].gate_act) {
     case SSM_ACT_SILU: return launch_bwd_t<T, TBC, SSM_ACT_SILU>(L, ndir, g, s, hook);
     case SSM_ACT_GELU: return launch_bwd_t<T, TBC, SSM_ACT_GELU>(L, ndir, g, s, hook);
@@ -615,7 +620,7 @@ static int launch_bwd_g(BwdLaunch& L, int ndir, const Geo& g, cudaStream_t s, co
 }
 
 static int launch_bwd(BwdLaunch& L, int ndir, const Geo& g, cudaStream_t s, const BwdHook* hook) {
-  if (ndir == 2 && L.dir[0].gate_act != L.dir[1].gate_act) {  // one launch per gate
+  if (ndir == 2 && (L.dir[0].gate_act != L.dir[1].gate_act || L.dir[0].has_z != L.dir[1].has_z)) {  // one launch per gate
     BwdLaunch L1 = L;
     L1.dir[0] = L.dir[1];
     if (L.ticket) {  // the second launch takes its tickets from the second direction's word
