@@ -6,6 +6,7 @@
 #include <cstring>
 #include <atomic>
 #include <mutex>
+#include <type_traits>
 
 #include "scan_bwd.cuh"
 #include "scan_fwd.cuh"
@@ -455,8 +456,13 @@ static int launch_fwd_t(FwdLaunch& L, int ndir, const Geo& g, cudaStream_t s) {
   L.ticket = nseg > 1 ? L.dir[0].seg_flag - 4 : nullptr;
   L.spin_limit = kLookbackSpin;
   const bool wide = (long)grid.x * grid.y * grid.z <= (long)(kFMinBlocks / 2) * kSMs;
-  auto kern = nseg > 1 ? (wide ? ssm_fwd_kernel<T, TBC, true, true> : ssm_fwd_kernel<T, TBC, false, true>)
-                       : (wide ? ssm_fwd_kernel<T, TBC, true, false> : ssm_fwd_kernel<T, TBC, false, false>);
+  const bool fast = ndir == 1 && !(L.dir[0].flags & SSM_REVERSE) && (L.dir[0].flags & SSM_DELTA_SOFTPLUS);
+  auto pick = [&](auto fast_c) {
+    constexpr bool F = decltype(fast_c)::value;
+    return nseg > 1 ? (wide ? ssm_fwd_kernel<T, TBC, true, true, F> : ssm_fwd_kernel<T, TBC, false, true, F>)
+                    : (wide ? ssm_fwd_kernel<T, TBC, true, false, F> : ssm_fwd_kernel<T, TBC, false, false, F>);
+  };
+  auto kern = fast ? pick(std::true_type{}) : pick(std::false_type{});
   SSM_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kBytes),
                  "cudaFuncSetAttribute(ssm_fwd_kernel)");
   kern<<<grid, kFThreads, kBytes, s>>>(L);

@@ -61,7 +61,9 @@ struct FwdSmem {
 // WIDE: the grid fills at most half the resident CTAs, so each thread may use
 // up to twice the registers (more scheduling freedom).
 // SEG: the launch cuts the sequence into segments (lookback code compiled in).
-template <typename T, typename TBC, bool WIDE, bool SEG>
+// FAST: a single-direction forward-frame launch with softplus(dt), those flags
+// being compile-time constants.
+template <typename T, typename TBC, bool WIDE, bool SEG, bool FAST>
 __global__ void __launch_bounds__(kFThreads, WIDE ? kFMinBlocks / 2 : kFMinBlocks) ssm_fwd_kernel(const __grid_constant__ FwdLaunch P) {
   using S = FwdSmem<T, TBC>;
   extern __shared__ __align__(1024) unsigned char smem[];
@@ -90,10 +92,10 @@ __global__ void __launch_bounds__(kFThreads, WIDE ? kFMinBlocks / 2 : kFMinBlock
   const int c = c0 + cl;
   const int L = a.L, Dm = a.Dm;
   if (c0 >= Dm) return;
-  const bool rev = (a.flags & SSM_REVERSE) != 0;
+  const bool rev = !FAST && (a.flags & SSM_REVERSE) != 0;
   const bool comp = rev && (a.flags & SSM_COMPLEMENT);
   const bool aligned = (a.flags & SSM_ALIGNED_SKIP) != 0;
-  const bool softplus = (a.flags & SSM_DELTA_SOFTPLUS) != 0;
+  const bool softplus = FAST || (a.flags & SSM_DELTA_SOFTPLUS) != 0;
   const bool has_z = a.has_z != 0, has_D = a.D != nullptr;
   const bool need_uo = has_D && rev && !aligned;
   const int nblk = (L + kChunk - 1) / kChunk;
