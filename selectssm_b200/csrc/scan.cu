@@ -456,7 +456,8 @@ static int launch_fwd_t(FwdLaunch& L, int ndir, const Geo& g, cudaStream_t s) {
   L.ticket = nseg > 1 ? L.dir[0].seg_flag - 4 : nullptr;
   L.spin_limit = kLookbackSpin;
   const bool wide = (long)grid.x * grid.y * grid.z <= (long)(kFMinBlocks / 2) * kSMs;
-  const bool fast = ndir == 1 && !(L.dir[0].flags & SSM_REVERSE) && (L.dir[0].flags & SSM_DELTA_SOFTPLUS);
+  const bool fast = ndir == 1 && !(L.dir[0].flags & SSM_REVERSE) && (L.dir[0].flags & SSM_DELTA_SOFTPLUS) &&
+                    g.L % kChunk == 0 && g.Dm % kTileCh == 0;
   auto pick = [&](auto fast_c) {
     constexpr bool F = decltype(fast_c)::value;
     return nseg > 1 ? (wide ? ssm_fwd_kernel<T, TBC, true, true, F> : ssm_fwd_kernel<T, TBC, false, true, F>)
@@ -590,7 +591,8 @@ static int launch_bwd_t(BwdLaunch& L, int ndir, const Geo& g, cudaStream_t s, co
   const int nseg = L.dir[0].nseg;
   dim3 grid((g.Dm + kBTile - 1) / kBTile, g.B, 1);
   const BwdDir& d0 = L.dir[0];
-  const bool fast = ndir == 1 && !(d0.flags & SSM_REVERSE) && (d0.flags & SSM_DELTA_SOFTPLUS);
+  const bool fast = ndir == 1 && !(d0.flags & SSM_REVERSE) && (d0.flags & SSM_DELTA_SOFTPLUS) &&
+                    g.L % kChunk == 0 && g.Dm % kBTile == 0;
   const bool mc = d0.bc_mode == kBcMulticast;
   auto kern = mc ? (fast ? ssm_bwd_kernel<T, TBC, G, true, true> : ssm_bwd_kernel<T, TBC, G, true, false>)
                  : (fast ? ssm_bwd_kernel<T, TBC, G, false, true> : ssm_bwd_kernel<T, TBC, G, false, false>);

@@ -61,8 +61,9 @@ struct FwdSmem {
 // WIDE: the grid fills at most half the resident CTAs, so each thread may use
 // up to twice the registers (more scheduling freedom).
 // SEG: the launch cuts the sequence into segments (lookback code compiled in).
-// FAST: a single-direction forward-frame launch with softplus(dt), those flags
-// being compile-time constants.
+// FAST: a single-direction forward-frame launch with softplus(dt), a length of
+// whole 16-step chunks and whole channel tiles: frame, softplus and bounds
+// masks are compile-time constants.
 template <typename T, typename TBC, bool WIDE, bool SEG, bool FAST>
 __global__ void __launch_bounds__(kFThreads, WIDE ? kFMinBlocks / 2 : kFMinBlocks) ssm_fwd_kernel(const __grid_constant__ FwdLaunch P) {
   using S = FwdSmem<T, TBC>;
@@ -103,7 +104,7 @@ __global__ void __launch_bounds__(kFThreads, WIDE ? kFMinBlocks / 2 : kFMinBlock
   const int j0 = seg * a.seg_chunks;
   const int j1 = min(nblk, j0 + a.seg_chunks);
   const int nloc = j1 - j0;
-  const bool cvalid = c < Dm;
+  const bool cvalid = FAST || c < Dm;
   const int co = comp ? Dm - 1 - c : c;
   const int oc0 = comp ? Dm - kTileCh - c0 : c0;
   // Loads: first the aggregate pass over the segment (segments that a later
@@ -178,7 +179,7 @@ __global__ void __launch_bounds__(kFThreads, WIDE ? kFMinBlocks / 2 : kFMinBlock
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       const int tl = 4 * i + nq;
-      const bool valid = j * kChunk + tl < L;
+      const bool valid = FAST || j * kChunk + tl < L;
       const float x = ld_f(su + tl * kTileCh + cl);
       const float dr = ld_f(sd + tl * kTileCh + cl) + bias;
       float dt = softplus ? softplus_f(dr) : dr;
@@ -243,7 +244,7 @@ __global__ void __launch_bounds__(kFThreads, WIDE ? kFMinBlocks / 2 : kFMinBlock
           const float xs = need_uo ? ld_f(suo + row * kTileCh + col) : ld_f(su + tl * kTileCh + cl);
           float y = fmaf(Dsk, xs, yv[i]);
           if (G >= 0) y *= act_f(ld_f(sz + row * kTileCh + col), G);
-          if (t < L && cvalid) st_act(out + ((size_t)b * L + l) * a.out_stride + co, y);
+          if (FAST || (t < L && cvalid)) st_act(out + ((size_t)b * L + l) * a.out_stride + co, y);
         }
       };
       switch (has_z ? a.gate_act : -1) {
