@@ -594,8 +594,13 @@ static int launch_bwd_t(BwdLaunch& L, int ndir, const Geo& g, cudaStream_t s, co
   const bool fast = ndir == 1 && !(d0.flags & SSM_REVERSE) && (d0.flags & SSM_DELTA_SOFTPLUS) &&
                     g.L % kChunk == 0 && g.Dm % kBTile == 0;
   const bool mc = d0.bc_mode == kBcMulticast;
-  auto kern = mc ? (fast ? ssm_bwd_kernel<T, TBC, G, true, true> : ssm_bwd_kernel<T, TBC, G, true, false>)
-                 : (fast ? ssm_bwd_kernel<T, TBC, G, false, true> : ssm_bwd_kernel<T, TBC, G, false, false>);
+  // fast launches have instances with and without the segment code; the
+  // generic instance always carries it
+  const bool seg = nseg > 1;
+  auto kern = mc ? (fast ? (seg ? ssm_bwd_kernel<T, TBC, G, true, true, true> : ssm_bwd_kernel<T, TBC, G, true, true, false>)
+                         : ssm_bwd_kernel<T, TBC, G, true, false, true>)
+                 : (fast ? (seg ? ssm_bwd_kernel<T, TBC, G, false, true, true> : ssm_bwd_kernel<T, TBC, G, false, true, false>)
+                         : ssm_bwd_kernel<T, TBC, G, false, false, true>);
   SSM_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes),
                  "cudaFuncSetAttribute(ssm_bwd_kernel)");
   L.zdiv = nseg;

@@ -169,14 +169,15 @@ __device__ __forceinline__ void tmem_wait_ld_regs(uint32_t (&r)[16]) {
 // the step loops hold no branch on it.
 // MC: dB / dC partial sums go to NVLink multicast addresses (cross-GPU sum);
 // a template parameter so the single-GPU instance carries no trace of it.
-template <typename T, typename TBC, int G, bool MC, bool FAST>
+// SEG: segment code (ticket, aggregate pass, carry chain) compiled in.
+template <typename T, typename TBC, int G, bool MC, bool FAST, bool SEG>
 __global__ void __launch_bounds__(kBThreads, 2) ssm_bwd_kernel(const __grid_constant__ BwdLaunch P) {
   extern __shared__ __align__(1024) unsigned char smem[];
   // CTA identity: with segments, from an atomic ticket in scan order (the last
   // segments first, so every segment a CTA waits for is already running);
   // otherwise from the block index.  Grid: (channel tiles, batch, directions x segments).
   int tile = blockIdx.x, b = blockIdx.y, dz = blockIdx.z;
-  if (P.ticket) {
+  if (SEG && P.ticket) {
     int* slot = reinterpret_cast<int*>(smem + BwdLayout::kTicketSlot);
     if (threadIdx.x == 0) *slot = atomicAdd(P.ticket, 1) + P.ticket_base;
     __syncthreads();
@@ -236,7 +237,7 @@ __global__ void __launch_bounds__(kBThreads, 2) ssm_bwd_kernel(const __grid_cons
   // Loads: first the aggregate pass over the segment (segments that a later
   // CTA waits for; delta, C, dout, z only), then the main pass, each visiting
   // the chunks last to first; load g uses stage g % 2.
-  const bool lookback = a.nseg > 1;
+  const bool lookback = SEG && a.nseg > 1;
   const int nagg = (lookback && seg > 0) ? nloc : 0;
   const int ntot = nagg + nloc;
   const uint32_t tx = BwdLayout::tx(sizeof(T), sizeof(TBC), has_z, mirror);
