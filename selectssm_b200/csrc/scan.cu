@@ -443,6 +443,12 @@ static int fill_fwd_dir(const ssm_params_t* p, const Geo& g, FwdDir* d, cudaStre
   return SSM_OK;
 }
 
+// Shapes and flags the frame-specialised ("fast") kernel instances serve:
+// softplus(dt), whole 16-step chunks, whole channel tiles.
+static bool fast_shape(const Geo& g, int tile, int flags) {
+  return (flags & SSM_DELTA_SOFTPLUS) && g.L % kChunk == 0 && g.Dm % tile == 0;
+}
+
 template <typename T, typename TBC>
 static int launch_fwd_t(FwdLaunch& L, int ndir, const Geo& g, cudaStream_t s) {
   constexpr int kBytes = FwdSmem<T, TBC>::kBytes;
@@ -456,14 +462,14 @@ static int launch_fwd_t(FwdLaunch& L, int ndir, const Geo& g, cudaStream_t s) {
   L.ticket = nseg > 1 ? L.dir[0].seg_flag - 4 : nullptr;
   L.spin_limit = kLookbackSpin;
   const bool wide = (long)grid.x * grid.y * grid.z <= (long)(kFMinBlocks / 2) * kSMs;
-  const bool fast = ndir == 1 && !(L.dir[0].flags & SSM_REVERSE) && (L.dir[0].flags & SSM_DELTA_SOFTPLUS) &&
-                    g.L % kChunk == 0 && g.Dm % kTileCh == 0;
-  auto pick = [&](auto fast_c) {
-    constexpr bool F = decltype(fast_c)::value;
+  const int fr = ndir == 1 && fast_shape(g, kTileCh, L.dir[0].flags) ? ((L.dir[0].flags & SSM_REVERSE) ? 2 : 1) : 0;
+  auto pick = [&](auto fr_c) {
+    constexpr int F = decltype(fr_c)::value;
     return nseg > 1 ? (wide ? ssm_fwd_kernel<T, TBC, true, true, F> : ssm_fwd_kernel<T, TBC, false, true, F>)
                     : (wide ? ssm_fwd_kernel<T, TBC, true, false, F> : ssm_fwd_kernel<T, TBC, false, false, F>);
   };
-  auto kern = fast ? pick(std::true_type{}) : pick(std::false_type{});
+  auto kern = fr == 1 ? pick(std::integral_constant<int, 1>{})
+                      : fr == 2 ? pick(std::integral_constant<int, 2>{}) : pick(std::integral_constant<int, 0>{});
   SSM_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kBytes),
                  "cudaFuncSetAttribute(ssm_fwd_kernel)");
   kern<<<grid, kFThreads, kBytes, s>>>(L);
@@ -472,8 +478,16 @@ static int launch_fwd_t(FwdLaunch& L, int ndir, const Geo& g, cudaStream_t s) {
   return SSM_OK;
 }
 
-// B / C always reach the kernels as float32 (bf16 rows are widened first)
+// B / C always reach the kernels as float32 (bf16 rows are widened first).
+// A bidirectional call whose directions can both run frame-specialised
+// instances runs them as two launches.
 static int launch_fwd(FwdLaunch& L, int ndir, const Geo& g, cudaStream_t s) {
+  if (ndir == 2 && fast_shape(g, kTileCh, L.dir[0].flags) && fast_shape(g, kTileCh, L.dir[1].flags)) {
+    FwdLaunch L1 = L;
+    L1.dir[0] = L.dir[1];
+    const int st = launch_fwd(L, 1, g, s);
+    return st ? st : launch_fwd(L1, 1, g, s);
+  }
   if (g.bf16) return launch_fwd_t<__nv_bfloat16, float>(L, ndir, g, s);
   return launch_fwd_t<float, float>(L, ndir, g, s);
 }
@@ -591,16 +605,21 @@ static int launch_bwd_t(BwdLaunch& L, int ndir, const Geo& g, cudaStream_t s, co
   const int nseg = L.dir[0].nseg;
   dim3 grid((g.Dm + kBTile - 1) / kBTile, g.B, 1);
   const BwdDir& d0 = L.dir[0];
-  const bool fast = ndir == 1 && !(d0.flags & SSM_REVERSE) && (d0.flags & SSM_DELTA_SOFTPLUS) &&
-                    g.L % kChunk == 0 && g.Dm % kBTile == 0;
+  const int fr = ndir == 1 && fast_shape(g, kBTile, d0.flags) ? ((d0.flags & SSM_REVERSE) ? 2 : 1) : 0;
   const bool mc = d0.bc_mode == kBcMulticast;
-  // fast launches have instances with and without the segment code; the
-  // generic instance always carries it
+  // The flavoured instances exist with and without the segment code; the
+  // generic one always carries it.  The multicast form (d_inner sharding) has
+  // no reverse-frame instance.
   const bool seg = nseg > 1;
-  auto kern = mc ? (fast ? (seg ? ssm_bwd_kernel<T, TBC, G, true, true, true> : ssm_bwd_kernel<T, TBC, G, true, true, false>)
-                         : ssm_bwd_kernel<T, TBC, G, true, false, true>)
-                 : (fast ? (seg ? ssm_bwd_kernel<T, TBC, G, false, true, true> : ssm_bwd_kernel<T, TBC, G, false, true, false>)
-                         : ssm_bwd_kernel<T, TBC, G, false, false, true>);
+  auto kern = ssm_bwd_kernel<T, TBC, G, false, 0, true>;
+  if (mc) {
+    kern = fr == 1 ? (seg ? ssm_bwd_kernel<T, TBC, G, true, 1, true> : ssm_bwd_kernel<T, TBC, G, true, 1, false>)
+                   : ssm_bwd_kernel<T, TBC, G, true, 0, true>;
+  } else if (fr == 1) {
+    kern = seg ? ssm_bwd_kernel<T, TBC, G, false, 1, true> : ssm_bwd_kernel<T, TBC, G, false, 1, false>;
+  } else if (fr == 2) {
+    kern = seg ? ssm_bwd_kernel<T, TBC, G, false, 2, true> : ssm_bwd_kernel<T, TBC, G, false, 2, false>;
+  }
   SSM_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes),
                  "cudaFuncSetAttribute(ssm_bwd_kernel)");
   L.zdiv = nseg;
@@ -633,7 +652,12 @@ static int launch_bwd_g(BwdLaunch& L, int ndir, const Geo& g, cudaStream_t s, co
 }
 
 static int launch_bwd(BwdLaunch& L, int ndir, const Geo& g, cudaStream_t s, const BwdHook* hook) {
-  if (ndir == 2 && (L.dir[0].gate_act != L.dir[1].gate_act || L.dir[0].has_z != L.dir[1].has_z)) {  // one launch per gate
+  // One launch per direction when the gates differ, or when both directions
+  // can run a frame-specialised instance (frame, softplus and masks
+  // compile-time), which beats sharing one generic launch.
+  if (ndir == 2 && (L.dir[0].gate_act != L.dir[1].gate_act || L.dir[0].has_z != L.dir[1].has_z ||
+                    (fast_shape(g, kBTile, L.dir[0].flags) && fast_shape(g, kBTile, L.dir[1].flags) &&
+                     L.dir[0].bc_mode != kBcMulticast))) {
     BwdLaunch L1 = L;
     L1.dir[0] = L.dir[1];
     if (L.ticket) {  // the second launch takes its tickets from the second direction's word

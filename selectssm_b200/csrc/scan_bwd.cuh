@@ -170,7 +170,7 @@ __device__ __forceinline__ void tmem_wait_ld_regs(uint32_t (&r)[16]) {
 // MC: dB / dC partial sums go to NVLink multicast addresses (cross-GPU sum);
 // a template parameter so the single-GPU instance carries no trace of it.
 // SEG: segment code (ticket, aggregate pass, carry chain) compiled in.
-template <typename T, typename TBC, int G, bool MC, bool FAST, bool SEG>
+template <typename T, typename TBC, int G, bool MC, int FR, bool SEG>
 __global__ void __launch_bounds__(kBThreads, 2) ssm_bwd_kernel(const __grid_constant__ BwdLaunch P) {
   extern __shared__ __align__(1024) unsigned char smem[];
   // CTA identity: with segments, from an atomic ticket in scan order (the last
@@ -197,12 +197,13 @@ __global__ void __launch_bounds__(kBThreads, 2) ssm_bwd_kernel(const __grid_cons
   const int c = c0 + cl;
   const int L = a.L, Dm = a.Dm;
   if (c0 >= Dm) return;
-  // FAST: a single-direction forward-frame launch with softplus(dt), whose
-  // length is a whole number of 16-step chunks and whose channels fill whole
-  // 128-channel tiles: frame, softplus and masks are compile-time constants, so
-  // the per-step code carries no frame-dependent address selects and no
-  // bounds predicates.  G < 0: no gate (z absent).
-  const bool rev = !FAST && (a.flags & SSM_REVERSE) != 0;
+  // FR: 1 (2) = a single-direction forward-frame (reverse-frame) launch with
+  // softplus(dt), whose length is a whole number of 16-step chunks and whose
+  // channels fill whole 128-channel tiles: frame, softplus and masks are
+  // compile-time constants, so the per-step code carries no frame-dependent
+  // address selects and no bounds predicates; 0 = generic.  G < 0: no gate.
+  constexpr bool FAST = FR != 0;
+  const bool rev = FR == 2 || (FR == 0 && (a.flags & SSM_REVERSE) != 0);
   const bool comp = rev && (a.flags & SSM_COMPLEMENT);
   const bool aligned = (a.flags & SSM_ALIGNED_SKIP) != 0;
   const bool softplus = FAST || (a.flags & SSM_DELTA_SOFTPLUS) != 0;

@@ -61,10 +61,10 @@ struct FwdSmem {
 // WIDE: the grid fills at most half the resident CTAs, so each thread may use
 // up to twice the registers (more scheduling freedom).
 // SEG: the launch cuts the sequence into segments (lookback code compiled in).
-// FAST: a single-direction forward-frame launch with softplus(dt), a length of
-// whole 16-step chunks and whole channel tiles: frame, softplus and bounds
-// masks are compile-time constants.
-template <typename T, typename TBC, bool WIDE, bool SEG, bool FAST>
+// FR: 1 (2) = a single-direction forward-frame (reverse-frame) launch with
+// softplus(dt), a length of whole 16-step chunks and whole channel tiles:
+// frame, softplus and bounds masks are compile-time constants; 0 = generic.
+template <typename T, typename TBC, bool WIDE, bool SEG, int FR>
 __global__ void __launch_bounds__(kFThreads, WIDE ? kFMinBlocks / 2 : kFMinBlocks) ssm_fwd_kernel(const __grid_constant__ FwdLaunch P) {
   using S = FwdSmem<T, TBC>;
   extern __shared__ __align__(1024) unsigned char smem[];
@@ -93,7 +93,8 @@ __global__ void __launch_bounds__(kFThreads, WIDE ? kFMinBlocks / 2 : kFMinBlock
   const int c = c0 + cl;
   const int L = a.L, Dm = a.Dm;
   if (c0 >= Dm) return;
-  const bool rev = !FAST && (a.flags & SSM_REVERSE) != 0;
+  constexpr bool FAST = FR != 0;
+  const bool rev = FR == 2 || (FR == 0 && (a.flags & SSM_REVERSE) != 0);
   const bool comp = rev && (a.flags & SSM_COMPLEMENT);
   const bool aligned = (a.flags & SSM_ALIGNED_SKIP) != 0;
   const bool softplus = FAST || (a.flags & SSM_DELTA_SOFTPLUS) != 0;
