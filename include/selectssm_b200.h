@@ -123,7 +123,10 @@ typedef struct ssm_params {
 
 /* Bytes of scratch (p->workspace) that ssm_fwd and ssm_bwd need for these
  * params: the forward uses it when it splits the sequence into segments, the
- * backward always; one buffer of this size serves both calls. */
+ * backward always; one buffer of this size serves both calls.  The scratch
+ * holds per-call partial sums and the segments' carry flags (reset by the
+ * call itself, on its stream), so two calls that may overlap on the GPU need
+ * separate workspaces. */
 SSM_API size_t ssm_workspace_bytes(const ssm_params_t* p);
 /* Bytes of scratch a single-direction backward needs for these params: ssm_bwd
  * (multicast = 0) or ssm_bwd_bc_multicast (multicast = 1, which keeps no dB /
