@@ -16,7 +16,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libselectssm_b200.so")
 SOURCES = ["scan.cu", "conv1d.cu", "noalloc.cu", "rmsnorm.cu", "selftest.cu"]
-HEADERS = ["common.cuh", "scan_kernels.cuh", "scan_bwd.cuh", "scan_fwd.cuh"]
+HEADERS = ["common.cuh", "scan_kernels.cuh", "scan_bwd.cuh", "scan_fwd.cuh", "scan_fwd_lane.cuh"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -10,6 +10,7 @@
 
 #include "scan_bwd.cuh"
 #include "scan_fwd.cuh"
+#include "scan_fwd_lane.cuh"
 
 namespace ssm {
 
@@ -396,7 +397,7 @@ static bool make_bc_maps(const ssm_params_t* p, const Geo& g, const float* Bw, c
 }
 
 // ---------------------------------------------------------------- forward launch
-static int fill_fwd_dir(const ssm_params_t* p, const Geo& g, FwdDir* d, cudaStream_t s) {
+static int fill_fwd_dir(const ssm_params_t* p, const Geo& g, FwdDir* d, cudaStream_t s, int box = kTileCh) {
   const uint64_t es = g.es;
   char* ws = static_cast<char*>(p->workspace);
   float* Bw = g.bcbf16 ? reinterpret_cast<float*>(ws + fwd_seg_bytes(g)) : nullptr;
@@ -405,12 +406,12 @@ static int fill_fwd_dir(const ssm_params_t* p, const Geo& g, FwdDir* d, cudaStre
     const int st = launch_widen_bc(p, g, Bw, Cw, s);
     if (st) return st;
   }
-  bool ok = make_map(&d->tm_u, p->u, g.bf16, g.Dm, g.L, g.B, g.Dm * es, (uint64_t)g.L * g.Dm * es, kTileCh, kChunk);
+  bool ok = make_map(&d->tm_u, p->u, g.bf16, g.Dm, g.L, g.B, g.Dm * es, (uint64_t)g.L * g.Dm * es, box, kChunk);
   ok = ok && make_map(&d->tm_delta, p->delta, g.bf16, g.Dm, g.L, g.B, g.Dm * es, (uint64_t)g.L * g.Dm * es,
-                      kTileCh, kChunk);
+                      box, kChunk);
   ok = ok && make_bc_maps(p, g, Bw, Cw, &d->tm_B, &d->tm_C);
   if (p->z)
-    ok = ok && make_map(&d->tm_z, p->z, g.bf16, g.Dm, g.L, g.B, g.zs * es, (uint64_t)g.L * g.zs * es, kTileCh,
+    ok = ok && make_map(&d->tm_z, p->z, g.bf16, g.Dm, g.L, g.B, g.zs * es, (uint64_t)g.L * g.zs * es, box,
                         kChunk);
   else
     std::memset(&d->tm_z, 0, sizeof(d->tm_z));
@@ -475,6 +476,37 @@ static int launch_fwd_t(FwdLaunch& L, int ndir, const Geo& g, cudaStream_t s) {
   kern<<<grid, kFThreads, kBytes, s>>>(L);
   note_launches(1);
   SSM_CUDA_CHECK(cudaGetLastError(), "launch ssm_fwd_kernel");
+  return SSM_OK;
+}
+
+// The one-lane-per-channel forward (scan_fwd_lane.cuh): single-direction,
+// forward-frame launches of the fast shape without segments, with enough
+// (batch row, channel) pairs to fill the GPU one lane each.
+static bool lane_fwd(const Geo& g, int flags) {
+#ifdef SSM_EXP_ENV
+  if (const char* e = getenv("SSM_LANE"))
+    if (atoi(e) == 0) return false;
+#endif
+  return g.ndir == 1 && !(flags & SSM_REVERSE) && fast_shape(g, kLTile, flags) &&
+         (long)g.B * g.Dm >= kLaneMinChannels && choose_segments(g, kFwdSeg).nseg == 1;
+}
+
+template <typename T>
+static int launch_fwd_lane_t(FwdLaunch& L, const Geo& g, cudaStream_t s) {
+  constexpr int kBytes = LaneSmem<T>::kBytes;
+  auto kern = ssm_fwd_lane_kernel<T, -1>;
+  switch (L.dir[0].has_z ? L.dir[0].gate_act : -1) {
+    case SSM_ACT_SILU: kern = ssm_fwd_lane_kernel<T, SSM_ACT_SILU>; break;
+    case SSM_ACT_GELU: kern = ssm_fwd_lane_kernel<T, SSM_ACT_GELU>; break;
+    case SSM_ACT_RELU: kern = ssm_fwd_lane_kernel<T, SSM_ACT_RELU>; break;
+    case SSM_ACT_NONE: kern = ssm_fwd_lane_kernel<T, SSM_ACT_NONE>; break;
+    default: break;
+  }
+  SSM_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kBytes),
+                 "cudaFuncSetAttribute(ssm_fwd_lane_kernel)");
+  kern<<<dim3(g.Dm / kLTile, g.B, 1), kLThreads, kBytes, s>>>(L);
+  note_launches(1);
+  SSM_CUDA_CHECK(cudaGetLastError(), "launch ssm_fwd_lane_kernel");
   return SSM_OK;
 }
 
@@ -764,6 +796,11 @@ int ssm_fwd_bidir(const ssm_params_t* fwd, const ssm_params_t* rev, ssm_stream_t
   FwdLaunch args;
   std::memset(&args, 0, sizeof(args));
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (lane_fwd(g, fwd->flags)) {
+    st = fill_fwd_dir(fwd, g, &args.dir[0], s, kLTile);
+    if (st) return st;
+    return g.bf16 ? launch_fwd_lane_t<__nv_bfloat16>(args, g, s) : launch_fwd_lane_t<float>(args, g, s);
+  }
   st = fill_fwd_dir(fwd, g, &args.dir[0], s);
   if (!st && rev) st = fill_fwd_dir(rev, g, &args.dir[1], s);
   if (st) return st;
