@@ -527,9 +527,13 @@ def measure(spec, args, world, rank, dev, lib, chan=False, bc_sum_mode="multicas
                 "unit": "GB/s", "traffic": read_traffic(f"ssm_bwd_kernel_{spec['key']}.md"),
                 "algorithmic_bytes": bb, "ms": t_bwd}
     roof_bwd["frac"] = roof_bwd["achieved"] / hbm
-    roof_fwd = {"kernel": "ssm_fwd call: ssm_fwd_kernel (+ segment pre-pass when segmented)", "bound": "hbm",
+    # the library's rule for its one-lane-per-channel forward (single direction, whole tiles and chunks)
+    lane = Bsz * D >= 65536 and L % 16 == 0 and D % 128 == 0
+    fwd_kernel = "ssm_fwd_lane_kernel" if lane else "ssm_fwd_kernel"
+    roof_fwd = {"kernel": f"ssm_fwd call: {fwd_kernel}" + (" (+ widen_bc_kernel for bf16 B/C)" if s == 2 else ""),
+                "bound": "hbm",
                 "achieved": fb / (t_fwd * 1e-3) / 1e9, "peak": hbm, "peak_source": src, "unit": "GB/s",
-                "traffic": read_traffic(f"ssm_fwd_kernel_{spec['key']}.md"), "algorithmic_bytes": fb, "ms": t_fwd}
+                "traffic": read_traffic(f"{fwd_kernel}_{spec['key']}.md"), "algorithmic_bytes": fb, "ms": t_fwd}
     roof_fwd["frac"] = roof_fwd["achieved"] / hbm
     step_roof = {"achieved": (fb + bb) / (ms * 1e-3) / 1e9, "peak": hbm, "peak_source": src, "unit": "GB/s",
                  "bytes_per_unit": (fb + bb) / units}
@@ -633,6 +637,7 @@ def main():
     ap.add_argument("--no-config2", action="store_true", help="skip the config-2 keys at N=1")
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--batch", type=int, default=None, help="override batch per GPU (small profiling cases)")
+    ap.add_argument("--seqlen", type=int, default=None, help="override the sequence length (small profiling cases)")
     ap.add_argument("--workload", type=int, default=5, choices=[2, 4, 5],
                     help="5 (default): the scaling workload, batch of 64 split over the ranks; 2: config 2 alone; "
                          "4: config 4 (with --parallel channels)")
@@ -653,6 +658,8 @@ def main():
             raise SystemExit("--config 3/4 time one GPU with the CUDA path only")
         return run_other_config(args)
     spec = SPECS[args.workload]
+    if args.seqlen:
+        spec = dict(spec, seqlen=args.seqlen)
     chan = args.parallel == "channels" and world > 1
     if args.impl == "reference":
         return reference_arm(spec, args, world, rank, chan)

@@ -14,7 +14,7 @@
 //   CTA  = one batch row b x 128 consecutive channels (4 warps); lane = channel.
 //   time = TMA stages of 16 steps (u, delta, z tiles of 128 ch x 16 steps; B and
 //          C rows of 16 x 16 float32, widened from bf16 beforehand when needed)
-//          in a ring of kLStages shared-memory stages completed on mbarriers;
+//          in a ring of two shared-memory stages completed on mbarriers;
 //          thread 0 refills a stage once all four warps released it.
 //   B and C rows are read as broadcast float4 loads (every lane of a warp
 //   reads the same row).
@@ -38,12 +38,6 @@ namespace ssm {
 #endif
 constexpr int kLTile = SSM_LANE_TILE;  // channels per CTA (one per thread)
 constexpr int kLThreads = kLTile;
-#ifndef SSM_LANE_POLY
-#define SSM_LANE_POLY 0
-#endif
-// State pairs (of 8) whose exponentials are evaluated on the FMA pipe by a
-// polynomial (ex2_poly2) instead of the special-function unit.
-constexpr int kLPoly = SSM_LANE_POLY;
 // Channels (batch rows x channels) from which the one-lane kernel is used:
 // below this the quad-per-channel kernel fills the GPU better.
 #ifndef SSM_LANE_MIN_CHANNELS
@@ -53,7 +47,7 @@ constexpr long kLaneMinChannels = SSM_LANE_MIN_CHANNELS;
 
 template <typename T>
 struct LaneSmem {
-  static constexpr int kStages = sizeof(T) == 2 ? 2 : 2;
+  static constexpr int kStages = 2;
   static constexpr int kAct = kChunk * kLTile * (int)sizeof(T);
   static constexpr int kBC = kChunk * kN * 4;
   static constexpr int kOffU = 0, kOffDelta = kAct, kOffZ = 2 * kAct, kOffB = 3 * kAct, kOffC = 3 * kAct + kBC;
@@ -154,7 +148,7 @@ __global__ void __launch_bounds__(kLThreads, lane_min_blocks<T>())
         for (int k = 0; k < 2; ++k) {
           const int p = 2 * q + k;
           const float2 e = fmul2(A2[p], dt2);
-          const float2 al = p < kLPoly ? ex2_poly2(e) : make_float2(ex2(e.x), ex2(e.y));
+          const float2 al = make_float2(ex2(e.x), ex2(e.y));
           const float2 Bp = k ? make_float2(Bv.z, Bv.w) : make_float2(Bv.x, Bv.y);
           const float2 Cp = k ? make_float2(Cv.z, Cv.w) : make_float2(Cv.x, Cv.y);
           h[p] = ffma2(al, h[p], fmul2(Bp, dx2));
