@@ -59,17 +59,40 @@ def alg_bytes(units, s, N, D):
     return fwd, bwd
 
 
-def read_traffic(name):
-    """dram bytes per launch recorded in a committed ncu summary, else None."""
+def read_profile(name, key="traffic_bytes_per_launch"):
+    """A per-launch figure recorded in a committed ncu summary (DRAM bytes by
+    default, or warp_instructions_per_launch), else None."""
     p = os.path.join(ROOT, "profiles", name)
     try:
         with open(p) as f:
             for line in f:
-                if line.startswith("traffic_bytes_per_launch:"):
+                if line.startswith(key + ":"):
                     return float(line.split(":", 1)[1])
     except OSError:
         pass
     return None
+
+
+def read_traffic(name):
+    return read_profile(name)
+
+
+SMS, SMSPS_PER_SM, MUFU_PER_SM_CLK = 148, 4, 16
+
+
+def compute_floor(ms, units, mufu_per_unit, profile, mhz):
+    """The kernel's compute-side floors at the sampled SM clock: special-function
+    (MUFU) operations at 16 per SM per clock, and warp instructions (from the
+    committed ncu count of the same launch) at one issue per scheduler per
+    clock.  The fractions say how close the call runs to each."""
+    hz = (mhz or 1965.0) * 1e6
+    mufu_ms = units * mufu_per_unit / (SMS * MUFU_PER_SM_CLK * hz) * 1e3
+    out = {"sm_mhz": mhz, "mufu_ops_per_unit": mufu_per_unit, "mufu_floor_ms": mufu_ms, "frac_of_mufu_floor": mufu_ms / ms}
+    inst = read_profile(profile, "warp_instructions_per_launch")
+    if inst:
+        issue_ms = inst / (SMS * SMSPS_PER_SM * hz) * 1e3
+        out.update({"warp_instructions": inst, "issue_floor_ms": issue_ms, "frac_of_issue_floor": issue_ms / ms})
+    return out
 
 
 class ClockSampler:
@@ -535,6 +558,11 @@ def measure(spec, args, world, rank, dev, lib, chan=False, bc_sum_mode="multicas
                 "achieved": fb / (t_fwd * 1e-3) / 1e9, "peak": hbm, "peak_source": src, "unit": "GB/s",
                 "traffic": read_traffic(f"{fwd_kernel}_{spec['key']}.md"), "algorithmic_bytes": fb, "ms": t_fwd}
     roof_fwd["frac"] = roof_fwd["achieved"] / hbm
+    # MUFU operations per unit: 16 state exponentials, softplus (ex2, lg2) and the silu gate (ex2, rcp) in the
+    # forward; the backward adds softplus' derivative (rcp) and recomputes the same 16 exponentials.
+    mhz = clk.summary().get("sm_mhz")
+    roof_fwd["compute"] = compute_floor(t_fwd, units, 20, f"{fwd_kernel}_{spec['key']}.md", mhz)
+    roof_bwd["compute"] = compute_floor(t_bwd, units, 21, f"ssm_bwd_kernel_{spec['key']}.md", mhz)
     step_roof = {"achieved": (fb + bb) / (ms * 1e-3) / 1e9, "peak": hbm, "peak_source": src, "unit": "GB/s",
                  "bytes_per_unit": (fb + bb) / units}
     step_roof["frac"] = step_roof["achieved"] / hbm
@@ -657,7 +685,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-config2", action="store_true", help="skip the config-2 keys at N=1")
-    ap.add_argument("--e2e-steps", type=int, default=10)
+    ap.add_argument("--e2e-steps", type=int, default=30)
     ap.add_argument("--batch", type=int, default=None, help="override batch per GPU (small profiling cases)")
     ap.add_argument("--seqlen", type=int, default=None, help="override the sequence length (small profiling cases)")
     ap.add_argument("--workload", type=int, default=5, choices=[2, 4, 5],
